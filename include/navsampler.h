@@ -1,0 +1,159 @@
+/*
+ * navsampler — sm_100a decode-time logits processing and token sampling.
+ *
+ * C ABI of the library (libnavsampler.so). Plain pointers and sizes only; the
+ * conventions follow the reference's native library Neuraval.Cuda.Native:
+ *   - exported symbols are `extern "C"` with default visibility
+ *     (Neuraval.Cuda.Native/src/navcuda.cu:9-13);
+ *   - status codes 0..7 keep NcbStatus's values (navcuda.cu:19-29), each entry
+ *     point returns its status AND records it for ncb_sampler_last_status()
+ *     (the g_lastStatus model, navcuda.cu:31-39, read by CudaDevice.ThrowIfError,
+ *     Neuraval.Cuda/CudaDevice.cs:70-91);
+ *   - `_device` entry points take device pointers and are asynchronous on the
+ *     given stream; host-array entry points copy in, launch, synchronise and
+ *     copy out (the navcuda.cu:702-734 pattern, without per-call allocation).
+ *
+ * Each sampling entry point replaces, for a [rows, vocab] fp32 batch, one call
+ * per row of TokenSampler.SampleNext (Neuraval/Generation/TokenSampler.cs:10);
+ * the LogitsProcessor entry points replace LogitsProcessor.* per row
+ * (Neuraval/Generation/LogitsProcessor.cs:8-114). There is no CPU fallback.
+ */
+#ifndef NAVSAMPLER_H
+#define NAVSAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define NCB_API __declspec(dllexport)
+#else
+#define NCB_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------
+ * 0..7 are NcbStatus (navcuda.cu:19-29). 8 is new: a size beyond what the
+ * handle was created for. */
+#define NCB_OK 0
+#define NCB_ERROR_NO_DEVICE 1
+#define NCB_ERROR_INIT_FAILED 2
+#define NCB_ERROR_ALLOC_FAILED 3
+#define NCB_ERROR_COPY_FAILED 4
+#define NCB_ERROR_LAUNCH_FAILED 5
+#define NCB_ERROR_NOT_INITIALIZED 6
+#define NCB_ERROR_INVALID_ARGUMENT 7
+#define NCB_ERROR_CAPACITY 8
+
+/* ---- per-row result flags (uint32 per row) -------------------------------
+ * Parity contract: a row's token equals the reference's unless one of the
+ * first three bits is set. */
+#define NCB_FLAG_DRAW_BOUNDARY 0x1u   /* u*retained within 1e-6*retained of S_j or S_{j-1} */
+#define NCB_FLAG_CUTOFF_BOUNDARY 0x2u /* top-p test S_i >= total*topP within 1e-6 relative */
+#define NCB_FLAG_TIE_AT_DRAW 0x4u     /* drawn position in a group of equal values: the C#
+                                         unstable sort (TokenSampler.cs:95) picks the id */
+#define NCB_FLAG_NONFINITE 0x8u       /* NaN/+inf value or no finite maximum: token -1 */
+#define NCB_FLAG_EXP_SLOW 0x10u       /* a weight needed the double-double exp path */
+#define NCB_FLAG_BAD_HISTORY 0x20u    /* row history longer than the handle's max: token -1 */
+
+/* ---- sampling options ----------------------------------------------------
+ * Mirrors GenerationOptions (Neuraval/Generation/GenerationOptions.cs:5-19):
+ * Greedy, Temperature, TopP, TopK, RepetitionPenalty. "No top-k" is any
+ * top_k >= vocab (GenerationOptions.CreateGreedy uses int.MaxValue, :79).
+ * frequency_penalty / presence_penalty are new (no reference counterpart):
+ * v - count*frequency - [count>0]*presence, after the repetition penalty and
+ * before the temperature scale; 0 disables them. */
+typedef struct NcbSamplerParams {
+    int32_t greedy;
+    float temperature;
+    float top_p;
+    int32_t top_k;
+    float repetition_penalty;
+    float frequency_penalty;
+    float presence_penalty;
+} NcbSamplerParams;
+
+typedef struct NcbSampler NcbSampler; /* opaque; owns device scratch only */
+
+/* GenerationOptions.Create's validation (GenerationOptions.cs:56-72): returns
+ * NCB_ERROR_INVALID_ARGUMENT for T<=0, top_p outside (0,1], top_k<=0,
+ * repetition_penalty<=0 or a NaN penalty. Host only; needs no device. */
+NCB_API int ncb_sampler_params_validate(const NcbSamplerParams* params);
+
+/* Creates a sampler bound to `device` with scratch for up to max_rows rows of
+ * up to max_vocab columns and histories of up to max_history ids per row.
+ * Replaces the per-call state of the C# sampler (HashSet, PriorityQueue,
+ * candidate list; TokenSampler.cs:61-95). The handle is single-stream: calls
+ * on one handle are serialised by a per-handle lock. */
+NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_history,
+                               NcbSampler** out);
+NCB_API int ncb_sampler_destroy(NcbSampler* sampler);
+
+/* TokenSampler.SampleNext (TokenSampler.cs:10-30) for `rows` rows at once.
+ *   d_logits      [rows, vocab] fp32, row-major, read only
+ *   d_hist        generated ids of all rows, concatenated (any int32 value;
+ *                 ids outside [0,vocab) never match, as with the C# HashSet)
+ *   d_hist_offsets rows+1 int32 offsets into d_hist (CSR)
+ *   d_uniforms    rows fp32 u in [0,1): the reference's (float)random.NextDouble()
+ *                 (TokenSampler.cs:125); unread when params->greedy
+ *   d_tokens      rows int32 out
+ *   d_flags       rows uint32 out (NCB_FLAG_*), may be NULL
+ *   d_probs       optional [rows, vocab] fp32 out: w_i/retained for the retained
+ *                 candidates, 0 elsewhere (unused when greedy), may be NULL
+ *   stream        cudaStream_t (NULL = legacy default stream)
+ * Asynchronous; arguments are validated on the host before any launch. */
+NCB_API int ncb_sample_rows_device(NcbSampler* sampler, const float* d_logits, int rows,
+                                   int vocab, const int32_t* d_hist,
+                                   const int32_t* d_hist_offsets, const float* d_uniforms,
+                                   const NcbSamplerParams* params, int32_t* d_tokens,
+                                   uint32_t* d_flags, float* d_probs, void* stream);
+
+/* Same with host arrays: copies in, samples, synchronises, copies out. This is
+ * the drop-in for TokenSampler.SampleNext(float[] logits, ...) with rows=1. */
+NCB_API int ncb_sample_rows(NcbSampler* sampler, const float* h_logits, int rows, int vocab,
+                            const int32_t* h_hist, const int32_t* h_hist_offsets,
+                            const float* h_uniforms, const NcbSamplerParams* params,
+                            int32_t* h_tokens, uint32_t* h_flags, float* h_probs);
+
+/* ---- LogitsProcessor, batched, in place on device [rows, vocab] ----------- */
+
+/* LogitsProcessor.ApplyRepetitionPenalty (LogitsProcessor.cs:8-36), per row
+ * with that row's CSR history. penalty<=0 -> NCB_ERROR_INVALID_ARGUMENT. */
+NCB_API int ncb_logits_repetition_penalty_device(NcbSampler* sampler, float* d_logits,
+                                                 int rows, int vocab, const int32_t* d_hist,
+                                                 const int32_t* d_hist_offsets,
+                                                 float penalty, void* stream);
+/* New (no reference counterpart): v - count*frequency - [count>0]*presence. */
+NCB_API int ncb_logits_frequency_presence_penalty_device(NcbSampler* sampler, float* d_logits,
+                                                         int rows, int vocab,
+                                                         const int32_t* d_hist,
+                                                         const int32_t* d_hist_offsets,
+                                                         float frequency, float presence,
+                                                         void* stream);
+/* LogitsProcessor.ApplyTemperature (LogitsProcessor.cs:38-51): divides by T. */
+NCB_API int ncb_logits_temperature_device(NcbSampler* sampler, float* d_logits, int rows,
+                                          int vocab, float temperature, void* stream);
+/* LogitsProcessor.FilterTopK (LogitsProcessor.cs:53-73): values below the
+ * top_k-th largest (with multiplicity) become -inf; no-op when top_k>=vocab. */
+NCB_API int ncb_logits_filter_top_k_device(NcbSampler* sampler, float* d_logits, int rows,
+                                           int vocab, int top_k, void* stream);
+/* LogitsProcessor.FilterTopP (LogitsProcessor.cs:75-114) on probabilities:
+ * keeps the smallest descending prefix whose sequential fp32 sum reaches top_p
+ * and renormalises it; d_flags (optional, rows) gets NCB_FLAG_TIE_AT_DRAW when
+ * the cutoff splits a group of equal probabilities. */
+NCB_API int ncb_logits_filter_top_p_device(NcbSampler* sampler, float* d_probs, int rows,
+                                           int vocab, float top_p, uint32_t* d_flags,
+                                           void* stream);
+
+/* ---- status --------------------------------------------------------------- */
+/* ncb_cuda_last_status / ncb_cuda_status_message (navcuda.cu:982-1001). */
+NCB_API int ncb_sampler_last_status(void);
+NCB_API const char* ncb_sampler_status_message(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NAVSAMPLER_H */

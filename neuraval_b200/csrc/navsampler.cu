@@ -1,0 +1,495 @@
+// navsampler: C ABI of the sm_100a sampling library (include/navsampler.h).
+//
+// Host-side conventions follow Neuraval.Cuda.Native/src/navcuda.cu: extern "C"
+// exports with default visibility (:9-13), NcbStatus codes (:19-29) and a
+// process-wide last status (:31-39, read through ncb_sampler_last_status as
+// CudaDevice.ThrowIfError does with ncb_cuda_last_status). Unlike navcuda's
+// global recursive mutex, a sampler handle carries its own lock, and the
+// host-array entry point reuses handle-owned device buffers instead of
+// allocating per call.
+#include "../../include/navsampler.h"
+
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "fullvocab_kernels.cuh"
+#include "logits_ops.cuh"
+#include "sampler_device.cuh"
+#include "topk_kernels.cuh"
+
+namespace {
+
+std::atomic<int> g_last_status{NCB_OK};
+
+int set_status(int st) {
+  g_last_status.store(st);
+  return st;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+int pow2_at_least(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+struct NcbSampler {
+  int device = 0;
+  int max_rows = 0, max_vocab = 0, max_history = 0;
+  int num_sms = 0;
+  int max_ctas = 0;
+  int max_smem_optin = 0;
+  std::mutex mu;
+  void* scratch = nullptr;
+  nvs::Scratch s{};
+  nvs::FvScratch fv{};
+  // host-array staging (allocated on first ncb_sample_rows call)
+  float* h_logits_dev = nullptr;
+  int32_t* h_hist_dev = nullptr;
+  int32_t* h_hoff_dev = nullptr;
+  float* h_u_dev = nullptr;
+  int32_t* h_tok_dev = nullptr;
+  uint32_t* h_flags_dev = nullptr;
+  float* h_probs_dev = nullptr;
+  size_t h_hist_cap = 0;
+  cudaStream_t host_stream = nullptr;
+};
+
+static bool params_ok(const NcbSamplerParams* p) {
+  if (!p) return false;
+  // GenerationOptions.Create (GenerationOptions.cs:56-72)
+  if (!(p->temperature > 0.0f)) return false;
+  if (!(p->top_p > 0.0f) || p->top_p > 1.0f) return false;
+  if (p->top_k <= 0) return false;
+  if (!(p->repetition_penalty > 0.0f)) return false;
+  if (p->frequency_penalty != p->frequency_penalty) return false;
+  if (p->presence_penalty != p->presence_penalty) return false;
+  return true;
+}
+
+static nvs::Params to_params(const NcbSamplerParams* p) {
+  nvs::Params q;
+  q.greedy = p->greedy;
+  q.temperature = p->temperature;
+  q.top_p = p->top_p;
+  q.top_k = p->top_k;
+  q.repetition_penalty = p->repetition_penalty;
+  q.frequency_penalty = p->frequency_penalty;
+  q.presence_penalty = p->presence_penalty;
+  return q;
+}
+
+// Column splits per row: enough CTAs to fill the GPU twice over when rows are
+// few, never a segment shorter than 8192 columns. NAVSAMPLER_SPLITS overrides
+// (tuning only).
+static int choose_splits(int rows, int V, int num_sms) {
+  int S = (2 * num_sms) / (rows > 0 ? rows : 1);
+  if (S < 1) S = 1;
+  int maxS = V / 8192;
+  if (maxS < 1) maxS = 1;
+  if (S > maxS) S = maxS;
+  if (const char* e = std::getenv("NAVSAMPLER_SPLITS")) {
+    int f = std::atoi(e);
+    if (f >= 1) S = f;
+  }
+  return S;
+}
+
+extern "C" {
+
+NCB_API int ncb_sampler_params_validate(const NcbSamplerParams* params) {
+  return set_status(params_ok(params) ? NCB_OK : NCB_ERROR_INVALID_ARGUMENT);
+}
+
+NCB_API int ncb_sampler_last_status(void) { return g_last_status.load(); }
+
+NCB_API const char* ncb_sampler_status_message(int status) {
+  switch (status) {
+    case NCB_OK: return "OK";
+    case NCB_ERROR_NO_DEVICE: return "no CUDA device";
+    case NCB_ERROR_INIT_FAILED: return "could not initialise the CUDA device";
+    case NCB_ERROR_ALLOC_FAILED: return "device allocation failed";
+    case NCB_ERROR_COPY_FAILED: return "host/device copy failed";
+    case NCB_ERROR_LAUNCH_FAILED: return "kernel launch failed";
+    case NCB_ERROR_NOT_INITIALIZED: return "sampler handle not initialised";
+    case NCB_ERROR_INVALID_ARGUMENT: return "invalid argument";
+    case NCB_ERROR_CAPACITY: return "size exceeds the sampler handle's capacity";
+    default: return "unknown status";
+  }
+}
+
+NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_history,
+                               NcbSampler** out) {
+  if (!out) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  *out = nullptr;
+  if (max_rows <= 0 || max_vocab <= 0 || max_history < 0 || device < 0)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0)
+    return set_status(NCB_ERROR_NO_DEVICE);
+  if (device >= count) return set_status(NCB_ERROR_NO_DEVICE);
+  DeviceGuard g(device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+
+  NcbSampler* h = new NcbSampler();
+  h->device = device;
+  h->max_rows = max_rows;
+  h->max_vocab = max_vocab;
+  h->max_history = max_history;
+  cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&h->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  h->max_ctas = max_rows > 2 * h->num_sms ? max_rows : 2 * h->num_sms;
+  // a single-row call may split into V/8192 segments
+  const int vsplits = max_vocab / 8192 + 1;
+  if (h->max_ctas < vsplits) h->max_ctas = vsplits;
+
+  // One scratch allocation, carved into aligned pieces.
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) / 256 * 256;
+    return o;
+  };
+  const size_t mc = (size_t)h->max_ctas;
+  const size_t o_cv = carve(mc * nvs::TK_CAPB * sizeof(float));
+  const size_t o_ci = carve(mc * nvs::TK_CAPB * sizeof(int32_t));
+  const size_t o_cn = carve(mc * sizeof(int32_t));
+  const size_t o_tk = carve((size_t)max_rows * sizeof(uint32_t));
+  const size_t o_rs = carve((size_t)max_rows * sizeof(uint32_t));
+  const size_t o_gv = carve(mc * sizeof(float));
+  const size_t o_gi = carve(mc * sizeof(int32_t));
+  const size_t o_er = carve(sizeof(uint32_t));
+  const size_t o_fx = carve((size_t)max_rows * sizeof(uint32_t));
+  const nvs::FvLayout fl = nvs::fv_layout(max_rows, max_vocab);
+  const size_t o_fv = carve(fl.total_bytes);
+  if (cudaMalloc(&h->scratch, off) != cudaSuccess) {
+    delete h;
+    return set_status(NCB_ERROR_ALLOC_FAILED);
+  }
+  char* b = static_cast<char*>(h->scratch);
+  h->s.cand_v = reinterpret_cast<float*>(b + o_cv);
+  h->s.cand_id = reinterpret_cast<int32_t*>(b + o_ci);
+  h->s.cand_n = reinterpret_cast<int32_t*>(b + o_cn);
+  h->s.tickets = reinterpret_cast<uint32_t*>(b + o_tk);
+  h->s.rowstate = reinterpret_cast<uint32_t*>(b + o_rs);
+  h->s.gv = reinterpret_cast<float*>(b + o_gv);
+  h->s.gi = reinterpret_cast<int32_t*>(b + o_gi);
+  h->s.error_word = reinterpret_cast<uint32_t*>(b + o_er);
+  h->s.fixup = reinterpret_cast<uint32_t*>(b + o_fx);
+  h->fv = nvs::fv_carve(b + o_fv, fl);
+  // tickets/rowstate/error word must start at zero; the kernels restore zero
+  if (cudaMemset(h->scratch, 0, off) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(h->scratch);
+    delete h;
+    return set_status(NCB_ERROR_INIT_FAILED);
+  }
+  *out = h;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_sampler_destroy(NcbSampler* h) {
+  if (!h) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  {
+    DeviceGuard g(h->device);
+    cudaDeviceSynchronize();
+    cudaFree(h->scratch);
+    cudaFree(h->h_logits_dev);
+    cudaFree(h->h_hist_dev);
+    cudaFree(h->h_hoff_dev);
+    cudaFree(h->h_u_dev);
+    cudaFree(h->h_tok_dev);
+    cudaFree(h->h_flags_dev);
+    cudaFree(h->h_probs_dev);
+    if (h->host_stream) cudaStreamDestroy(h->host_stream);
+  }
+  delete h;
+  return set_status(NCB_OK);
+}
+
+// Launches the sampling kernels for one batch; caller holds h->mu and the
+// device guard.
+static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
+                         const int32_t* d_hist, const int32_t* d_hoff, const float* d_u,
+                         const NcbSamplerParams* prm, int32_t* d_tok, uint32_t* d_flags,
+                         float* d_probs, cudaStream_t stream) {
+  if (rows == 0) return NCB_OK;
+  nvs::SampleArgs a{};
+  a.logits = d_logits;
+  a.V = V;
+  a.hist = d_hist;
+  a.hoff = d_hoff;
+  a.uniforms = d_u;
+  a.p = to_params(prm);
+  a.tokens = d_tok;
+  a.flags = d_flags;
+  a.probs = d_probs;
+  a.s = h->s;
+  const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
+  a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
+
+  if (prm->greedy) {
+    int S = choose_splits(rows, V, h->num_sms);
+    a.seg_len = round_up((V + S - 1) / S, 4);
+    S = (V + a.seg_len - 1) / a.seg_len;
+    a.bm_words = (a.seg_len + 31) / 32;
+    const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
+    if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
+    dim3 grid(S, rows);
+    if (counts) {
+      cudaFuncSetAttribute(nvs::greedy_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      nvs::greedy_kernel<true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+    } else {
+      cudaFuncSetAttribute(nvs::greedy_kernel<false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      nvs::greedy_kernel<false><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+    }
+    return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
+  }
+
+  const int K = prm->top_k < V ? prm->top_k : V;
+  if (K < V && K <= nvs::TK_KMAX) {
+    int S = choose_splits(rows, V, h->num_sms);
+    a.seg_len = round_up((V + S - 1) / S, 4);
+    S = (V + a.seg_len - 1) / a.seg_len;
+    if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
+    a.bm_words = (a.seg_len + 31) / 32;
+    const size_t smem = (size_t)nvs::TK_NSTAGE * nvs::TK_CHUNK * 4 + (size_t)nvs::TK_CAPB * 8 +
+                        256 * 4 + nvs::TK_NSTAGE * 8 + (size_t)a.bm_words * 4 +
+                        (size_t)a.h_cap * 4;
+    if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
+    dim3 grid(S, rows);
+    if (counts) {
+      cudaFuncSetAttribute(nvs::topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      nvs::topk_kernel<true><<<grid, nvs::TK_THREADS, smem, stream>>>(a);
+    } else {
+      cudaFuncSetAttribute(nvs::topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      nvs::topk_kernel<false><<<grid, nvs::TK_THREADS, smem, stream>>>(a);
+    }
+    if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    // rows whose ties overflowed the top-k buffers (normally none)
+    const int fst = nvs::launch_fullvocab(h->fv, a, rows, K, h->max_smem_optin, stream, true, 8);
+    return fst;
+  }
+
+  // Full-vocabulary nucleus (no effective top-k) and very large top-k.
+  return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_smem_optin, stream, false, 0);
+}
+
+static int validate_sample_args(NcbSampler* h, const void* logits, int rows, int vocab,
+                                const void* hist, const void* hoff, const void* u,
+                                const NcbSamplerParams* prm, const void* tok) {
+  if (!h) return NCB_ERROR_NOT_INITIALIZED;
+  if (!logits || !hoff || !tok || !prm) return NCB_ERROR_INVALID_ARGUMENT;
+  if (!params_ok(prm)) return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows < 0 || vocab <= 0) return NCB_ERROR_INVALID_ARGUMENT;
+  if (!prm->greedy && !u) return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NCB_ERROR_CAPACITY;
+  if ((reinterpret_cast<uintptr_t>(logits) & 3u) != 0u) return NCB_ERROR_INVALID_ARGUMENT;
+  (void)hist;
+  return NCB_OK;
+}
+
+NCB_API int ncb_sample_rows_device(NcbSampler* h, const float* d_logits, int rows, int vocab,
+                                   const int32_t* d_hist, const int32_t* d_hist_offsets,
+                                   const float* d_uniforms, const NcbSamplerParams* params,
+                                   int32_t* d_tokens, uint32_t* d_flags, float* d_probs,
+                                   void* stream) {
+  int st = validate_sample_args(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms,
+                                params, d_tokens);
+  if (st != NCB_OK) return set_status(st);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  st = launch_sample(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms, params,
+                     d_tokens, d_flags, d_probs, static_cast<cudaStream_t>(stream));
+  return set_status(st);
+}
+
+NCB_API int ncb_sample_rows(NcbSampler* h, const float* h_logits, int rows, int vocab,
+                            const int32_t* h_hist, const int32_t* h_hist_offsets,
+                            const float* h_uniforms, const NcbSamplerParams* params,
+                            int32_t* h_tokens, uint32_t* h_flags, float* h_probs) {
+  int st = validate_sample_args(h, h_logits, rows, vocab, h_hist, h_hist_offsets, h_uniforms,
+                                params, h_tokens);
+  if (st != NCB_OK) return set_status(st);
+  if (rows == 0) return set_status(NCB_OK);
+  const int64_t nh = h_hist_offsets[rows];
+  if (h_hist_offsets[0] != 0 || nh < 0 || (nh > 0 && !h_hist)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  for (int r = 0; r < rows; ++r)
+    if (h_hist_offsets[r + 1] < h_hist_offsets[r]) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  // lazily sized staging buffers owned by the handle
+  if (!h->h_logits_dev) {
+    const size_t nl = (size_t)h->max_rows * h->max_vocab;
+    if (cudaMalloc(&h->h_logits_dev, nl * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->h_hoff_dev, ((size_t)h->max_rows + 1) * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&h->h_u_dev, (size_t)h->max_rows * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->h_tok_dev, (size_t)h->max_rows * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&h->h_flags_dev, (size_t)h->max_rows * sizeof(uint32_t)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return set_status(NCB_ERROR_ALLOC_FAILED);
+  }
+  if ((size_t)nh > h->h_hist_cap) {
+    cudaFree(h->h_hist_dev);
+    h->h_hist_dev = nullptr;
+    size_t cap = (size_t)nh < 1024 ? 1024 : (size_t)nh;
+    if (cudaMalloc(&h->h_hist_dev, cap * sizeof(int32_t)) != cudaSuccess)
+      return set_status(NCB_ERROR_ALLOC_FAILED);
+    h->h_hist_cap = cap;
+  }
+  if (h_probs && !h->h_probs_dev) {
+    if (cudaMalloc(&h->h_probs_dev, (size_t)h->max_rows * h->max_vocab * sizeof(float)) != cudaSuccess)
+      return set_status(NCB_ERROR_ALLOC_FAILED);
+  }
+  cudaStream_t s = h->host_stream;
+  bool ok = cudaMemcpyAsync(h->h_logits_dev, h_logits, (size_t)rows * vocab * sizeof(float),
+                            cudaMemcpyHostToDevice, s) == cudaSuccess;
+  ok = ok && cudaMemcpyAsync(h->h_hoff_dev, h_hist_offsets, ((size_t)rows + 1) * sizeof(int32_t),
+                             cudaMemcpyHostToDevice, s) == cudaSuccess;
+  if (nh > 0)
+    ok = ok && cudaMemcpyAsync(h->h_hist_dev, h_hist, (size_t)nh * sizeof(int32_t),
+                               cudaMemcpyHostToDevice, s) == cudaSuccess;
+  if (!params->greedy)
+    ok = ok && cudaMemcpyAsync(h->h_u_dev, h_uniforms, (size_t)rows * sizeof(float),
+                               cudaMemcpyHostToDevice, s) == cudaSuccess;
+  if (!ok) return set_status(NCB_ERROR_COPY_FAILED);
+  st = launch_sample(h, h->h_logits_dev, rows, vocab, h->h_hist_dev, h->h_hoff_dev, h->h_u_dev,
+                     params, h->h_tok_dev, h->h_flags_dev, h_probs ? h->h_probs_dev : nullptr, s);
+  if (st != NCB_OK) return set_status(st);
+  ok = cudaMemcpyAsync(h_tokens, h->h_tok_dev, (size_t)rows * sizeof(int32_t),
+                       cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  if (h_flags)
+    ok = ok && cudaMemcpyAsync(h_flags, h->h_flags_dev, (size_t)rows * sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  if (h_probs)
+    ok = ok && cudaMemcpyAsync(h_probs, h->h_probs_dev, (size_t)rows * vocab * sizeof(float),
+                               cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  if (!ok) return set_status(NCB_ERROR_COPY_FAILED);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return set_status(NCB_ERROR_LAUNCH_FAILED);
+  return set_status(NCB_OK);
+}
+
+// ---- LogitsProcessor --------------------------------------------------------
+
+static int check_rows(NcbSampler* h, const void* x, int rows, int vocab) {
+  if (!h) return NCB_ERROR_NOT_INITIALIZED;
+  if (!x || rows < 0 || vocab <= 0) return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NCB_ERROR_CAPACITY;
+  return NCB_OK;
+}
+
+NCB_API int ncb_logits_repetition_penalty_device(NcbSampler* h, float* d_logits, int rows,
+                                                 int vocab, const int32_t* d_hist,
+                                                 const int32_t* d_hist_offsets, float penalty,
+                                                 void* stream) {
+  int st = check_rows(h, d_logits, rows, vocab);
+  if (st != NCB_OK) return set_status(st);
+  if (!d_hist_offsets || !(penalty > 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (penalty == 1.0f || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:17-18
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  const size_t smem = (size_t)((vocab + 31) / 32) * 4;
+  if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
+  cudaFuncSetAttribute(nvs::repetition_penalty_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  nvs::repetition_penalty_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+      d_logits, vocab, d_hist, d_hist_offsets, penalty);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+NCB_API int ncb_logits_frequency_presence_penalty_device(NcbSampler* h, float* d_logits,
+                                                         int rows, int vocab,
+                                                         const int32_t* d_hist,
+                                                         const int32_t* d_hist_offsets,
+                                                         float frequency, float presence,
+                                                         void* stream) {
+  int st = check_rows(h, d_logits, rows, vocab);
+  if (st != NCB_OK) return set_status(st);
+  if (!d_hist_offsets || frequency != frequency || presence != presence)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if ((frequency == 0.0f && presence == 0.0f) || rows == 0) return set_status(NCB_OK);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  const int h_cap = pow2_at_least(h->max_history > 0 ? h->max_history : 1);
+  const size_t smem = (size_t)h_cap * 4;
+  if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
+  cudaFuncSetAttribute(nvs::frequency_presence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  nvs::frequency_presence_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+      d_logits, vocab, d_hist, d_hist_offsets, frequency, presence, h_cap, nullptr);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+NCB_API int ncb_logits_temperature_device(NcbSampler* h, float* d_logits, int rows, int vocab,
+                                          float temperature, void* stream) {
+  int st = check_rows(h, d_logits, rows, vocab);
+  if (st != NCB_OK) return set_status(st);
+  if (!(temperature > 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (temperature == 1.0f || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:44-45
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  const size_t n = (size_t)rows * vocab;
+  const int grid = 4 * h->num_sms;
+  if ((reinterpret_cast<uintptr_t>(d_logits) & 15u) == 0u)
+    nvs::temperature_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, n, temperature);
+  else
+    nvs::temperature_kernel_unaligned<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, n,
+                                                                                         temperature);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+NCB_API int ncb_logits_filter_top_k_device(NcbSampler* h, float* d_logits, int rows, int vocab,
+                                           int top_k, void* stream) {
+  int st = check_rows(h, d_logits, rows, vocab);
+  if (st != NCB_OK) return set_status(st);
+  if (top_k <= 0) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (top_k >= vocab || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:62-63
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  nvs::filter_top_k_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, vocab, top_k);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+NCB_API int ncb_logits_filter_top_p_device(NcbSampler* h, float* d_probs, int rows, int vocab,
+                                           float top_p, uint32_t* d_flags, void* stream) {
+  int st = check_rows(h, d_probs, rows, vocab);
+  if (st != NCB_OK) return set_status(st);
+  if (!(top_p > 0.0f) || top_p > 1.0f) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (top_p >= 1.0f || rows == 0) {  // LogitsProcessor.cs:84-85
+    if (d_flags && rows > 0 && cudaMemsetAsync(d_flags, 0, (size_t)rows * 4, s) != cudaSuccess)
+      return set_status(NCB_ERROR_LAUNCH_FAILED);
+    return set_status(NCB_OK);
+  }
+  const size_t smem = (size_t)nvs::FV_GCAP * 16 + (size_t)(2 * nvs::FV_NB + 1) * 4;
+  cudaFuncSetAttribute(nvs::filter_top_p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  nvs::filter_top_p_kernel<<<rows, nvs::FV_THREADS, smem, s>>>(d_probs, vocab, top_p, d_flags, h->fv);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+}  // extern "C"

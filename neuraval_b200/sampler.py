@@ -1,0 +1,123 @@
+"""Handle-owning front end over the C ABI: one CudaTokenSampler per device.
+
+Mirrors the host class a Neuraval.Cuda caller would hold (CudaBuffer-style
+ownership, Neuraval.Cuda/CudaBuffer.cs:5-82): the handle owns device scratch,
+the caller owns every input and output buffer. Device-pointer methods take
+torch CUDA tensors (torch is only the allocator and stream provider here);
+host methods take numpy arrays.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import native
+from .native import NcbSamplerParams, check, load, make_params
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(ctypes.c_void_p)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        return None
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+class CudaTokenSampler:
+    """Batched TokenSampler.SampleNext / LogitsProcessor on one GPU."""
+
+    def __init__(self, device: int = 0, max_rows: int = 1, max_vocab: int = 32000,
+                 max_history: int = 4096):
+        self._lib = load()
+        h = ctypes.c_void_p()
+        check(self._lib.ncb_sampler_create(device, max_rows, max_vocab, max_history,
+                                           ctypes.byref(h)), "ncb_sampler_create")
+        self._h = h
+        self.device = device
+        self.max_rows, self.max_vocab, self.max_history = max_rows, max_vocab, max_history
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            check(self._lib.ncb_sampler_destroy(self._h), "ncb_sampler_destroy")
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- sampling -------------------------------------------------------
+    def sample_rows_device(self, logits, hist_ids, hist_offsets, uniforms,
+                           params: NcbSamplerParams, tokens, flags=None, probs=None,
+                           stream=None) -> None:
+        """Asynchronous: all tensors on this sampler's device."""
+        rows, vocab = int(logits.shape[0]), int(logits.shape[1])
+        st = self._lib.ncb_sample_rows_device(
+            self._h, _ptr(logits), rows, vocab, _ptr(hist_ids), _ptr(hist_offsets),
+            _ptr(uniforms), ctypes.byref(params), _ptr(tokens), _ptr(flags), _ptr(probs),
+            _stream_ptr(stream))
+        check(st, "ncb_sample_rows_device")
+
+    def sample_rows(self, logits: np.ndarray, hist_ids: np.ndarray, hist_offsets: np.ndarray,
+                    uniforms: np.ndarray, params: NcbSamplerParams, want_probs: bool = False):
+        """Host arrays in and out (copies, samples, synchronises)."""
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        rows, vocab = logits.shape
+        hist = np.ascontiguousarray(hist_ids, dtype=np.int32)
+        offs = np.ascontiguousarray(hist_offsets, dtype=np.int32)
+        uni = np.ascontiguousarray(uniforms, dtype=np.float32)
+        tokens = np.zeros(rows, dtype=np.int32)
+        flags = np.zeros(rows, dtype=np.uint32)
+        probs = np.zeros((rows, vocab), dtype=np.float32) if want_probs else None
+        st = self._lib.ncb_sample_rows(self._h, _ptr(logits), rows, vocab,
+                                       _ptr(hist) if hist.size else None, _ptr(offs), _ptr(uni),
+                                       ctypes.byref(params), _ptr(tokens), _ptr(flags),
+                                       _ptr(probs))
+        check(st, "ncb_sample_rows")
+        return tokens, flags, probs
+
+    # ---- LogitsProcessor (in place, device tensors) ----------------------
+    def repetition_penalty_(self, logits, hist_ids, hist_offsets, penalty, stream=None):
+        check(self._lib.ncb_logits_repetition_penalty_device(
+            self._h, _ptr(logits), int(logits.shape[0]), int(logits.shape[1]), _ptr(hist_ids),
+            _ptr(hist_offsets), ctypes.c_float(penalty), _stream_ptr(stream)),
+            "repetition_penalty")
+
+    def frequency_presence_penalty_(self, logits, hist_ids, hist_offsets, frequency, presence,
+                                    stream=None):
+        check(self._lib.ncb_logits_frequency_presence_penalty_device(
+            self._h, _ptr(logits), int(logits.shape[0]), int(logits.shape[1]), _ptr(hist_ids),
+            _ptr(hist_offsets), ctypes.c_float(frequency), ctypes.c_float(presence),
+            _stream_ptr(stream)), "frequency_presence_penalty")
+
+    def temperature_(self, logits, temperature, stream=None):
+        check(self._lib.ncb_logits_temperature_device(
+            self._h, _ptr(logits), int(logits.shape[0]), int(logits.shape[1]),
+            ctypes.c_float(temperature), _stream_ptr(stream)), "temperature")
+
+    def filter_top_k_(self, logits, top_k, stream=None):
+        check(self._lib.ncb_logits_filter_top_k_device(
+            self._h, _ptr(logits), int(logits.shape[0]), int(logits.shape[1]), int(top_k),
+            _stream_ptr(stream)), "filter_top_k")
+
+    def filter_top_p_(self, probs, top_p, flags=None, stream=None):
+        check(self._lib.ncb_logits_filter_top_p_device(
+            self._h, _ptr(probs), int(probs.shape[0]), int(probs.shape[1]),
+            ctypes.c_float(top_p), _ptr(flags), _stream_ptr(stream)), "filter_top_p")
+
+
+__all__ = ["CudaTokenSampler", "NcbSamplerParams", "make_params", "native"]
