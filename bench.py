@@ -160,7 +160,7 @@ def cpu_baseline(wl, seconds):
     one = sub / (time.perf_counter() - t0)
     rows = 0
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds and rows < 50 * B:
+    while time.perf_counter() - t0 < seconds and rows < 2000 * B:
         pyoracle.sample_rows(wl["logits"], wl["hist_ids"], offs, wl["uniforms"], p,
                              exp_mode=pyoracle.EXP_GLIBC, threads=threads)
         rows += B
@@ -239,17 +239,36 @@ def main():
     flags = torch.empty(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(i):
+    def step(i, stream):
         sampler.sample_rows_device(bufs[i % NBUF], hist, offs, u, params, tokens, flags,
                                    None, stream)
 
+    cur = torch.cuda.current_stream(dev)
     for i in range(max(3, args.warmup)):
-        step(i)
+        step(i, cur)
     torch.cuda.synchronize()
 
-    # device-resident throughput: CUDA events on the launching stream
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+    # eager launches (each call goes through ctypes): reported for reference
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for i in range(args.steps):
+        step(i, cur)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1)
+
+    # timed region: the K steps captured once in a CUDA graph and replayed, so the
+    # device timeline holds only the sampling kernels (no host launch gaps)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(cur)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(args.steps):
+                step(i, torch.cuda.current_stream(dev))
+    torch.cuda.synchronize()
+    graph.replay()  # one untimed replay
+    torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -257,42 +276,44 @@ def main():
     with clocks:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
-        for i in range(args.steps):
-            ev[i][0].record(stream)
-            step(i)
-            ev[i][1].record(stream)
-        t_end.record(stream)
+        t_start.record(cur)
+        graph.replay()
+        t_end.record(cur)
         torch.cuda.synchronize()
     total_ms = t_start.elapsed_time(t_end)
-    per_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    per_launch_ms = total_ms / args.steps
     if world > 1:
-        t = torch.tensor([total_ms, per_launch_ms], device=dev)
+        t = torch.tensor([total_ms, per_launch_ms, eager_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms, per_launch_ms = float(t[0]), float(t[1])
+        total_ms, per_launch_ms, eager_ms = float(t[0]), float(t[1]), float(t[2])
     value = world * B * args.steps / (total_ms / 1e3)
+    del graph
 
     # end to end through the host-array entry point (pinned host buffers)
-    h_logits = torch.from_numpy(wl["logits"]).pin_memory().numpy()
-    h_hist = torch.from_numpy(wl["hist_ids"]).pin_memory().numpy()
-    h_offs = torch.from_numpy(wl["hist_offsets"]).pin_memory().numpy()
-    h_u = torch.from_numpy(wl["uniforms"]).pin_memory().numpy()
-    for _ in range(2):
-        sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
-    if world > 1:
-        torch.distributed.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t[0])
-    e2e = {"value": world * B * args.e2e_steps / e2e_s, "unit": UNIT,
-           "h2d_bytes_per_step": int(h_logits.nbytes + h_hist.nbytes + h_offs.nbytes + h_u.nbytes),
-           "d2h_bytes_per_step": int(B * 4 * 2),
-           "api": "ncb_sample_rows (host arrays; copies in, samples, synchronises, copies out)"}
+    e2e = None
+    if args.e2e_steps > 0:
+        h_logits = torch.from_numpy(wl["logits"]).pin_memory().numpy()
+        h_hist = torch.from_numpy(wl["hist_ids"]).pin_memory().numpy()
+        h_offs = torch.from_numpy(wl["hist_offsets"]).pin_memory().numpy()
+        h_u = torch.from_numpy(wl["uniforms"]).pin_memory().numpy()
+        for _ in range(2):
+            sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
+        e2e_s = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        e2e = {"value": world * B * args.e2e_steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": int(h_logits.nbytes + h_hist.nbytes + h_offs.nbytes +
+                                         h_u.nbytes),
+               "d2h_bytes_per_step": int(B * 4 * 2),
+               "api": "ncb_sample_rows (host arrays; copies in, samples, synchronises, "
+                      "copies out)"}
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -310,8 +331,10 @@ def main():
                             "algorithmic_bytes_per_launch": bytes_per_launch},
                "e2e": e2e,
                "gpu_launches": 2 * args.steps,
+               "eager_value": world * B * args.steps / (eager_ms / 1e3),
+               "timing": "CUDA events around one replay of a CUDA graph holding the K steps",
                "clocks": clocks.summary()}
-        if world == 1:
+        if world == 1 and args.cpu_seconds > 0:
             v, cores, sample, one = cpu_baseline(wl, args.cpu_seconds)
             out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                                    "sample": sample, "single_thread_value": one}

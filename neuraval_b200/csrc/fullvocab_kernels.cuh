@@ -775,28 +775,17 @@ inline int launch_fullvocab(const FvScratch& f, SampleArgs a, int rows, int K, i
                             cudaStream_t stream, bool fixup, int fixup_ctas) {
   if (a.V > f.max_vocab) return 8;  // NCB_ERROR_CAPACITY
   a.seg_len = a.V;
-  a.bm_words = (a.V + 31) / 32;
+  a.bm_words = (a.V + 31) / 32 + 1;
   const bool counts = (a.p.frequency_penalty != 0.0f || a.p.presence_penalty != 0.0f);
   const size_t smem = fv_smem_bytes(a.bm_words, counts ? a.h_cap : 0);
   if ((int)smem > max_smem) return 8;
   if (fixup) {
     const int g = rows < fixup_ctas ? rows : fixup_ctas;
-    if (counts) {
-      cudaFuncSetAttribute(fullvocab_fixup_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      fullvocab_fixup_kernel<true><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
-    } else {
-      cudaFuncSetAttribute(fullvocab_fixup_kernel<false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      fullvocab_fixup_kernel<false><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
-    }
+    if (counts) fullvocab_fixup_kernel<true><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
+    else fullvocab_fixup_kernel<false><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
   } else if (counts) {
-    cudaFuncSetAttribute(fullvocab_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
     fullvocab_kernel<true><<<rows, FV_THREADS, smem, stream>>>(a, f, K);
   } else {
-    cudaFuncSetAttribute(fullvocab_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
     fullvocab_kernel<false><<<rows, FV_THREADS, smem, stream>>>(a, f, K);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 5;

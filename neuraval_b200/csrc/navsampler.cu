@@ -33,7 +33,12 @@ struct DeviceGuard {
   bool ok = false;
   explicit DeviceGuard(int dev) {
     if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    ok = cudaSetDevice(dev) == cudaSuccess;
+    if (prev == dev) {
+      prev = -1;  // nothing to restore
+      ok = true;
+    } else {
+      ok = cudaSetDevice(dev) == cudaSuccess;
+    }
   }
   ~DeviceGuard() {
     if (prev >= 0) cudaSetDevice(prev);
@@ -55,6 +60,7 @@ struct NcbSampler {
   int num_sms = 0;
   int max_ctas = 0;
   int max_smem_optin = 0;
+  int forced_splits = 0;  // NAVSAMPLER_SPLITS at creation (tuning only)
   std::mutex mu;
   void* scratch = nullptr;
   nvs::Scratch s{};
@@ -98,17 +104,36 @@ static nvs::Params to_params(const NcbSamplerParams* p) {
 // Column splits per row: enough CTAs to fill the GPU twice over when rows are
 // few, never a segment shorter than 8192 columns. NAVSAMPLER_SPLITS overrides
 // (tuning only).
-static int choose_splits(int rows, int V, int num_sms) {
+static int choose_splits(int rows, int V, int num_sms, int forced) {
+  if (forced >= 1) return forced;
   int S = (2 * num_sms) / (rows > 0 ? rows : 1);
   if (S < 1) S = 1;
   int maxS = V / 8192;
   if (maxS < 1) maxS = 1;
   if (S > maxS) S = maxS;
-  if (const char* e = std::getenv("NAVSAMPLER_SPLITS")) {
-    int f = std::atoi(e);
-    if (f >= 1) S = f;
-  }
   return S;
+}
+
+// The dynamic shared memory limit of every kernel is raised once per handle
+// (a per-function attribute), not on every call.
+static bool raise_smem_limits(int limit) {
+  bool ok = true;
+  auto set = [&](const void* fn) {
+    ok = ok && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, limit) ==
+                   cudaSuccess;
+  };
+  set((const void*)nvs::topk_kernel<true>);
+  set((const void*)nvs::topk_kernel<false>);
+  set((const void*)nvs::greedy_kernel<true>);
+  set((const void*)nvs::greedy_kernel<false>);
+  set((const void*)nvs::fullvocab_kernel<true>);
+  set((const void*)nvs::fullvocab_kernel<false>);
+  set((const void*)nvs::fullvocab_fixup_kernel<true>);
+  set((const void*)nvs::fullvocab_fixup_kernel<false>);
+  set((const void*)nvs::filter_top_p_kernel);
+  set((const void*)nvs::repetition_penalty_kernel);
+  set((const void*)nvs::frequency_presence_kernel);
+  return ok;
 }
 
 extern "C" {
@@ -154,7 +179,10 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->max_history = max_history;
   cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
   cudaDeviceGetAttribute(&h->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (const char* e = std::getenv("NAVSAMPLER_SPLITS")) h->forced_splits = std::atoi(e);
   h->max_ctas = max_rows > 2 * h->num_sms ? max_rows : 2 * h->num_sms;
+  if (h->forced_splits > 0 && (size_t)max_rows * h->forced_splits > (size_t)h->max_ctas)
+    h->max_ctas = max_rows * h->forced_splits;
   // a single-row call may split into V/8192 segments
   const int vsplits = max_vocab / 8192 + 1;
   if (h->max_ctas < vsplits) h->max_ctas = vsplits;
@@ -194,7 +222,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->s.fixup = reinterpret_cast<uint32_t*>(b + o_fx);
   h->fv = nvs::fv_carve(b + o_fv, fl);
   // tickets/rowstate/error word must start at zero; the kernels restore zero
-  if (cudaMemset(h->scratch, 0, off) != cudaSuccess ||
+  if (!raise_smem_limits(h->max_smem_optin) || cudaMemset(h->scratch, 0, off) != cudaSuccess ||
       cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(h->scratch);
     delete h;
@@ -245,20 +273,16 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
 
   if (prm->greedy) {
-    int S = choose_splits(rows, V, h->num_sms);
+    int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);
     S = (V + a.seg_len - 1) / a.seg_len;
-    a.bm_words = (a.seg_len + 31) / 32;
+    a.bm_words = (a.seg_len + 31) / 32 + 1;
     const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
     if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
     dim3 grid(S, rows);
     if (counts) {
-      cudaFuncSetAttribute(nvs::greedy_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
       nvs::greedy_kernel<true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
     } else {
-      cudaFuncSetAttribute(nvs::greedy_kernel<false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       nvs::greedy_kernel<false><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
     }
     return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
@@ -266,23 +290,19 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
 
   const int K = prm->top_k < V ? prm->top_k : V;
   if (K < V && K <= nvs::TK_KMAX) {
-    int S = choose_splits(rows, V, h->num_sms);
+    int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);
     S = (V + a.seg_len - 1) / a.seg_len;
     if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
-    a.bm_words = (a.seg_len + 31) / 32;
+    a.bm_words = (a.seg_len + 31) / 32 + 1;
     const size_t smem = (size_t)nvs::TK_NSTAGE * nvs::TK_CHUNK * 4 + (size_t)nvs::TK_CAPB * 8 +
                         256 * 4 + nvs::TK_NSTAGE * 8 + (size_t)a.bm_words * 4 +
                         (size_t)a.h_cap * 4;
     if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
     dim3 grid(S, rows);
     if (counts) {
-      cudaFuncSetAttribute(nvs::topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
       nvs::topk_kernel<true><<<grid, nvs::TK_THREADS, smem, stream>>>(a);
     } else {
-      cudaFuncSetAttribute(nvs::topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
       nvs::topk_kernel<false><<<grid, nvs::TK_THREADS, smem, stream>>>(a);
     }
     if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
@@ -412,8 +432,6 @@ NCB_API int ncb_logits_repetition_penalty_device(NcbSampler* h, float* d_logits,
   DeviceGuard g(h->device);
   const size_t smem = (size_t)((vocab + 31) / 32) * 4;
   if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
-  cudaFuncSetAttribute(nvs::repetition_penalty_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
   nvs::repetition_penalty_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
       d_logits, vocab, d_hist, d_hist_offsets, penalty);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
@@ -435,8 +453,6 @@ NCB_API int ncb_logits_frequency_presence_penalty_device(NcbSampler* h, float* d
   const int h_cap = pow2_at_least(h->max_history > 0 ? h->max_history : 1);
   const size_t smem = (size_t)h_cap * 4;
   if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
-  cudaFuncSetAttribute(nvs::frequency_presence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
   nvs::frequency_presence_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
       d_logits, vocab, d_hist, d_hist_offsets, frequency, presence, h_cap, nullptr);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
@@ -486,8 +502,6 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* h, float* d_probs, int ro
     return set_status(NCB_OK);
   }
   const size_t smem = (size_t)nvs::FV_GCAP * 16 + (size_t)(2 * nvs::FV_NB + 1) * 4;
-  cudaFuncSetAttribute(nvs::filter_top_p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
   nvs::filter_top_p_kernel<<<rows, nvs::FV_THREADS, smem, s>>>(d_probs, vocab, top_p, d_flags, h->fv);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
 }

@@ -177,6 +177,14 @@ __device__ __forceinline__ int count_in_sorted(const int32_t* a, int n, int32_t 
   return lo - first;
 }
 
+// Penalty bits of ids col..col+3 (the bitmap has one spare word at the end).
+__device__ __forceinline__ uint32_t penalty_bits4(const Penalty& P, int col) {
+  const int rel = col - P.c0;
+  const int w = rel >> 5, sh = rel & 31;
+  const uint64_t win = (uint64_t)P.bitmap[w] | ((uint64_t)P.bitmap[w + 1] << 32);
+  return (uint32_t)(win >> sh) & 0xFu;
+}
+
 // Value before the temperature scale.
 __device__ __forceinline__ float adjust(const Penalty& P, float l, int id) {
   float v = l;

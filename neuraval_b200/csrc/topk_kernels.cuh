@@ -51,7 +51,7 @@ struct SampleArgs {
   int32_t* tokens;
   uint32_t* flags;
   float* probs;
-  int bm_words;         // bitmap words per CTA
+  int bm_words;         // bitmap words per CTA (columns/32 rounded up, plus one spare)
   int h_cap;            // history ids per CTA in smem (counts only), power of 2
   Scratch s;
 };
@@ -75,7 +75,7 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
   P.rep = (P.pen != 1.0f) && H > 0;
   P.cnt = kCounts && (P.freq != 0.0f || P.pres != 0.0f) && H > 0;
   if (!P.rep && !P.cnt) return true;
-  const int words = (c1 - c0 + 31) >> 5;
+  const int words = ((c1 - c0 + 31) >> 5) + 1;  // one spare word for 4-id windows
   for (int i = threadIdx.x; i < words; i += blockDim.x) bitmap[i] = 0u;
   if (threadIdx.x == 0) *s_hn = 0;
   __syncthreads();
@@ -423,36 +423,53 @@ __global__ void __launch_bounds__(TK_THREADS, 2) topk_kernel(SampleArgs a) {
       const int nq = len >> 2;
       const int base = a0 + t * TK_CHUNK;
       float4* sq = reinterpret_cast<float4*>(stage + st * TK_CHUNK);
-      const uint32_t theta = s_theta;
+      const float theta = kval(s_theta);
 #pragma unroll
       for (int k = 0; k < TK_CHUNK / 4 / TK_THREADS; ++k) {
         const int q = tid + k * TK_THREADS;
         const bool valid = q < nq;
-        float4 x = valid ? sq[q] : make_float4(0.f, 0.f, 0.f, 0.f);
         const int col = base + 4 * q;
-        float vv[4] = {x.x, x.y, x.z, x.w};
-        bool cand[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float v = canon(__fmul_rn(adjust(P, vv[j], col + j), scale));
-          if (valid && (v != v || v == INFINITY)) {
-            s_nonfinite = 1;
-            v = -INFINITY;
+        float vv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        bool any = false;
+        if (valid) {
+          const float4 x = sq[q];
+          vv[0] = __fmul_rn(x.x, scale);
+          vv[1] = __fmul_rn(x.y, scale);
+          vv[2] = __fmul_rn(x.z, scale);
+          vv[3] = __fmul_rn(x.w, scale);
+          if ((P.rep || P.cnt) && penalty_bits4(P, col) != 0u) {
+            // a penalised id among the four: exact per-element path
+            vv[0] = __fmul_rn(adjust(P, x.x, col), scale);
+            vv[1] = __fmul_rn(adjust(P, x.y, col + 1), scale);
+            vv[2] = __fmul_rn(adjust(P, x.z, col + 2), scale);
+            vv[3] = __fmul_rn(adjust(P, x.w, col + 3), scale);
           }
-          vv[j] = v;
-          cand[j] = valid && fkey(v) >= theta;
+          // NaN or +inf: !(v < inf); -inf is a legal value
+          if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
+              !(vv[3] < INFINITY))
+            s_nonfinite = 1;
+          any = vv[0] >= theta || vv[1] >= theta || vv[2] >= theta || vv[3] >= theta;
         }
-        if (valid) sq[q] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        if (__any_sync(0xffffffffu, any)) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) warp_append(cand[j], vv[j], col + j, cv, cid, &s_count, &s_overflow);
+          for (int j = 0; j < 4; ++j) {
+            const bool c = any && vv[j] >= theta;
+            warp_append(c, canon(vv[j]), col + j, cv, cid, &s_count, &s_overflow);
+          }
+        }
       }
       __syncthreads();
       if (s_overflow) {
         // exact K-th largest of (earlier candidates) + (this chunk)
         const int nb = s_cnt_before;
-        const float* sv = stage + st * TK_CHUNK;
-        const uint32_t key = cta_kth_largest_key([&](int i) { return cv[i]; }, nb,
-                                                 [&](int i) { return sv[i]; }, len, K, hist, s_sh);
+        const float* sraw = stage + st * TK_CHUNK;
+        // staged values are raw logits: recompute exactly as the fast path does
+        auto sval = [&](int i) -> float {
+          const float v = canon(__fmul_rn(adjust(P, sraw[i], base + i), scale));
+          return (v < INFINITY) ? v : -INFINITY;
+        };
+        const uint32_t key = cta_kth_largest_key([&](int i) { return cv[i]; }, nb, sval, len, K,
+                                                 hist, s_sh);
         constexpr int PER = TK_CAPB / TK_THREADS;
         float rv[PER];
         int rid[PER];
@@ -475,8 +492,9 @@ __global__ void __launch_bounds__(TK_THREADS, 2) topk_kernel(SampleArgs a) {
         for (int k = 0; k < PER; ++k) warp_append(keep[k], rv[k], rid[k], cv, cid, &s_count, &s_overflow);
         for (int i0 = 0; i0 < len; i0 += TK_THREADS) {
           const int i = i0 + tid;
-          const bool ok = i < len && fkey(sv[i]) >= key;
-          warp_append(ok, ok ? sv[i] : 0.f, base + i, cv, cid, &s_count, &s_overflow);
+          const float v = i < len ? sval(i) : -INFINITY;
+          const bool ok = i < len && fkey(v) >= key;
+          warp_append(ok, v, base + i, cv, cid, &s_count, &s_overflow);
         }
         __syncthreads();
         if (tid == 0 && s_overflow) {

@@ -96,12 +96,14 @@ def test_vocab_sharded_workload_single_gpu(gpu_sampler, oracle):
 
 
 @pytest.mark.parametrize("splits", ["1", "3", "7", "16"])
-def test_column_splits_merge(gpu_sampler, oracle, monkeypatch, splits):
-    monkeypatch.setenv("NAVSAMPLER_SPLITS", splits)
-    wl = workloads.zipf_ranked(B=24, V=50000, H=300, seed=9)
-    full_check(gpu_sampler, oracle, wl, label=f"splits={splits}")
-    wl = workloads.peaked_head(B=24, V=50000, seed=5, greedy=True)
-    full_check(gpu_sampler, oracle, wl, probs=False, label=f"greedy splits={splits}")
+def test_column_splits_merge(navlib, oracle, monkeypatch, splits):
+    from neuraval_b200.sampler import CudaTokenSampler
+    monkeypatch.setenv("NAVSAMPLER_SPLITS", splits)  # read when the handle is created
+    with CudaTokenSampler(0, max_rows=32, max_vocab=50000, max_history=512) as s:
+        wl = workloads.zipf_ranked(B=24, V=50000, H=300, seed=9)
+        full_check(s, oracle, wl, label=f"splits={splits}")
+        wl = workloads.peaked_head(B=24, V=50000, seed=5, greedy=True)
+        full_check(s, oracle, wl, probs=False, label=f"greedy splits={splits}")
 
 
 def _edge_rows(V, rng):
@@ -119,7 +121,7 @@ def _edge_rows(V, rng):
     rows.append(r)
     r = rng.standard_normal(V).astype(np.float32)
     r[0] = -0.0
-    r[1] = 0.0
+    r[1:2] = 0.0
     r[2:] = -1
     rows.append(r)
     return np.stack(rows)
