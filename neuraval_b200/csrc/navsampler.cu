@@ -60,6 +60,7 @@ struct NcbSampler {
   int num_sms = 0;
   int max_ctas = 0;
   int max_smem_optin = 0;
+  int max_dyn_smem = 0;  // dynamic shared memory a launch may request (opt-in minus static)
   int forced_splits = 0;  // NAVSAMPLER_SPLITS at creation (tuning only)
   std::mutex mu;
   void* scratch = nullptr;
@@ -119,7 +120,14 @@ static int choose_splits(int rows, int V, int num_sms, int forced) {
 static bool raise_smem_limits(int limit) {
   bool ok = true;
   auto set = [&](const void* fn) {
-    ok = ok && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, limit) ==
+    // static + dynamic shared memory may not exceed the opt-in limit
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) {
+      ok = false;
+      return;
+    }
+    const int dyn = limit - (int)fa.sharedSizeBytes;
+    ok = ok && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) ==
                    cudaSuccess;
   };
   set((const void*)nvs::topk_kernel<true>);
@@ -179,6 +187,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->max_history = max_history;
   cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
   cudaDeviceGetAttribute(&h->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  h->max_dyn_smem = h->max_smem_optin - 4096;  // every kernel uses < 4 KiB of static smem
   if (const char* e = std::getenv("NAVSAMPLER_SPLITS")) h->forced_splits = std::atoi(e);
   h->max_ctas = max_rows > 2 * h->num_sms ? max_rows : 2 * h->num_sms;
   if (h->forced_splits > 0 && (size_t)max_rows * h->forced_splits > (size_t)h->max_ctas)
@@ -278,7 +287,7 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     S = (V + a.seg_len - 1) / a.seg_len;
     a.bm_words = (a.seg_len + 31) / 32 + 1;
     const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
-    if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
     dim3 grid(S, rows);
     if (counts) {
       nvs::greedy_kernel<true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
@@ -298,7 +307,7 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     const size_t smem = (size_t)nvs::TK_NSTAGE * nvs::TK_CHUNK * 4 + (size_t)nvs::TK_CAPB * 8 +
                         256 * 4 + nvs::TK_NSTAGE * 8 + (size_t)a.bm_words * 4 +
                         (size_t)a.h_cap * 4;
-    if ((int)smem > h->max_smem_optin) return NCB_ERROR_CAPACITY;
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
     dim3 grid(S, rows);
     if (counts) {
       nvs::topk_kernel<true><<<grid, nvs::TK_THREADS, smem, stream>>>(a);
@@ -307,12 +316,12 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     }
     if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
     // rows whose ties overflowed the top-k buffers (normally none)
-    const int fst = nvs::launch_fullvocab(h->fv, a, rows, K, h->max_smem_optin, stream, true, 8);
+    const int fst = nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, true, 8);
     return fst;
   }
 
   // Full-vocabulary nucleus (no effective top-k) and very large top-k.
-  return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_smem_optin, stream, false, 0);
+  return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, false, 0);
 }
 
 static int validate_sample_args(NcbSampler* h, const void* logits, int rows, int vocab,
@@ -431,7 +440,7 @@ NCB_API int ncb_logits_repetition_penalty_device(NcbSampler* h, float* d_logits,
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard g(h->device);
   const size_t smem = (size_t)((vocab + 31) / 32) * 4;
-  if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
+  if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
   nvs::repetition_penalty_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
       d_logits, vocab, d_hist, d_hist_offsets, penalty);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
@@ -452,7 +461,7 @@ NCB_API int ncb_logits_frequency_presence_penalty_device(NcbSampler* h, float* d
   DeviceGuard g(h->device);
   const int h_cap = pow2_at_least(h->max_history > 0 ? h->max_history : 1);
   const size_t smem = (size_t)h_cap * 4;
-  if ((int)smem > h->max_smem_optin) return set_status(NCB_ERROR_CAPACITY);
+  if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
   nvs::frequency_presence_kernel<<<rows, nvs::LP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
       d_logits, vocab, d_hist, d_hist_offsets, frequency, presence, h_cap, nullptr);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
