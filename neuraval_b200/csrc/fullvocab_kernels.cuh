@@ -34,6 +34,7 @@ constexpr int FV_THREADS = 1024;
 constexpr int FV_NB = 4096;          // value bins over x in [-17, 0]
 constexpr int FV_GCAP = 4096;        // keys per group sorted in shared memory
 constexpr float FV_XMIN = -17.0f;    // exp(-17) < 2^-24
+constexpr int FV_FIXUP_MAX_LIST = 1024;
 
 struct FvLayout {
   size_t comp_bytes, sum_bytes, total_bytes;
@@ -564,10 +565,22 @@ template <bool kCounts>
 __global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(SampleArgs a, FvScratch f,
                                                                         int K, int rows) {
   extern __shared__ __align__(128) unsigned char smem[];
-  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
-    if (a.s.fixup[row] == 0u) continue;
-    fullvocab_row<kCounts>(a, f, K, row, smem);
-    if (threadIdx.x == 0) a.s.fixup[row] = 0u;
+  __shared__ int s_list[FV_FIXUP_MAX_LIST];
+  __shared__ int s_n;
+  // one parallel pass collects the marked rows (no dependent loads per row)
+  for (int base = 0; base < rows; base += FV_FIXUP_MAX_LIST) {
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    for (int r = base + threadIdx.x; r < min(rows, base + FV_FIXUP_MAX_LIST); r += blockDim.x)
+      if (a.s.fixup[r] != 0u && (r % gridDim.x) == blockIdx.x) s_list[atomicAdd(&s_n, 1)] = r;
+    __syncthreads();
+    const int n = s_n;
+    for (int i = 0; i < n; ++i) {
+      const int row = s_list[i];
+      fullvocab_row<kCounts>(a, f, K, row, smem);
+      if (threadIdx.x == 0) a.s.fixup[row] = 0u;
+      __syncthreads();
+    }
   }
 }
 

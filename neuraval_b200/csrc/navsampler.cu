@@ -18,6 +18,7 @@
 #include "logits_ops.cuh"
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
+#include "topk_warp_kernel.cuh"
 
 namespace {
 
@@ -132,6 +133,8 @@ static bool raise_smem_limits(int limit) {
   };
   set((const void*)nvs::topk_kernel<true>);
   set((const void*)nvs::topk_kernel<false>);
+  set((const void*)nvs::topk_warp_kernel<true>);
+  set((const void*)nvs::topk_warp_kernel<false>);
   set((const void*)nvs::greedy_kernel<true>);
   set((const void*)nvs::greedy_kernel<false>);
   set((const void*)nvs::fullvocab_kernel<true>);
@@ -298,6 +301,20 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   }
 
   const int K = prm->top_k < V ? prm->top_k : V;
+  if (K < V && K <= nvs::TW_KMAX) {
+    int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
+    a.seg_len = round_up((V + S - 1) / S, 4);
+    S = (V + a.seg_len - 1) / a.seg_len;
+    if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
+    a.bm_words = (a.seg_len + 31) / 32 + 1;
+    const size_t smem = nvs::tw_smem_bytes(a.bm_words, a.h_cap);
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+    dim3 grid(S, rows);
+    if (counts) nvs::topk_warp_kernel<true><<<grid, nvs::TW_THREADS, smem, stream>>>(a);
+    else nvs::topk_warp_kernel<false><<<grid, nvs::TW_THREADS, smem, stream>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, true, 8);
+  }
   if (K < V && K <= nvs::TK_KMAX) {
     int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);

@@ -423,7 +423,8 @@ __global__ void __launch_bounds__(TK_THREADS, 2) topk_kernel(SampleArgs a) {
       const int nq = len >> 2;
       const int base = a0 + t * TK_CHUNK;
       float4* sq = reinterpret_cast<float4*>(stage + st * TK_CHUNK);
-      const float theta = kval(s_theta);
+      const uint32_t tkey = s_theta;
+      const float theta = tkey == 0u ? -INFINITY : kval(tkey);  // key 0: accept everything
 #pragma unroll
       for (int k = 0; k < TK_CHUNK / 4 / TK_THREADS; ++k) {
         const int q = tid + k * TK_THREADS;
