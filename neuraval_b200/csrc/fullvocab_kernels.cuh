@@ -553,7 +553,7 @@ __device__ void fullvocab_row(const SampleArgs& a, const FvScratch& f, int K, in
 
 // One CTA per row.
 template <bool kCounts>
-__global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_kernel(SampleArgs a, FvScratch f, int K) {
+__global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_kernel(const __grid_constant__ SampleArgs a, FvScratch f, int K) {
   extern __shared__ __align__(128) unsigned char smem[];
   fullvocab_row<kCounts>(a, f, K, blockIdx.x, smem);
 }
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_kernel(SampleArgs a, 
 // path, every row the top-k kernel marked (ties at the k-th value overflowing
 // its candidate buffers). Unmarked rows cost one load.
 template <bool kCounts>
-__global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(SampleArgs a, FvScratch f,
+__global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(const __grid_constant__ SampleArgs a, FvScratch f,
                                                                         int K, int rows) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_list[FV_FIXUP_MAX_LIST];

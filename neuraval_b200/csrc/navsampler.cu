@@ -345,9 +345,10 @@ static int validate_sample_args(NcbSampler* h, const void* logits, int rows, int
                                 const void* hist, const void* hoff, const void* u,
                                 const NcbSamplerParams* prm, const void* tok) {
   if (!h) return NCB_ERROR_NOT_INITIALIZED;
-  if (!logits || !hoff || !tok || !prm) return NCB_ERROR_INVALID_ARGUMENT;
-  if (!params_ok(prm)) return NCB_ERROR_INVALID_ARGUMENT;
+  if (!prm || !params_ok(prm)) return NCB_ERROR_INVALID_ARGUMENT;
   if (rows < 0 || vocab <= 0) return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows == 0) return NCB_OK;  // an empty batch needs no buffers
+  if (!logits || !hoff || !tok) return NCB_ERROR_INVALID_ARGUMENT;
   if (!prm->greedy && !u) return NCB_ERROR_INVALID_ARGUMENT;
   if (rows > h->max_rows || vocab > h->max_vocab) return NCB_ERROR_CAPACITY;
   if ((reinterpret_cast<uintptr_t>(logits) & 3u) != 0u) return NCB_ERROR_INVALID_ARGUMENT;

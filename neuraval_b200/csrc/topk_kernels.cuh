@@ -131,7 +131,7 @@ __device__ __forceinline__ Best warp_best(Best b) {
 }
 
 template <bool kCounts>
-__global__ void __launch_bounds__(GR_THREADS) greedy_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem);
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
@@ -333,7 +333,7 @@ __device__ void finish_row(const SampleArgs& a, int row, const float* cv, const 
 }
 
 template <bool kCounts>
-__global__ void __launch_bounds__(TK_THREADS, 2) topk_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(TK_THREADS, 2) topk_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* stage = reinterpret_cast<float*>(smem);                 // [NSTAGE][CHUNK]
   float* cv = stage + TK_NSTAGE * TK_CHUNK;                       // [CAPB]

@@ -73,8 +73,8 @@ __device__ __forceinline__ void warp_sort128_desc(uint64_t (&k)[4]) {
 // K-th (a sorted prefix), and returns the new count; theta_w becomes the K-th
 // value. When the kept prefix would leave no room for another ballot of 32,
 // *tie_overflow is set.
-__device__ __forceinline__ int warp_compact(float* wv, int* wi, int count, int K, float& theta_w,
-                                            bool& tie_overflow) {
+__device__ __noinline__ int warp_compact(float* wv, int* wi, int count, int K, float& theta_w,
+                                         bool& tie_overflow) {
   const int lane = threadIdx.x & 31;
   uint64_t k[4];
 #pragma unroll
@@ -112,21 +112,36 @@ __device__ __forceinline__ int warp_compact(float* wv, int* wi, int count, int K
   return keep;
 }
 
+// Per-warp stream state, kept in shared memory so the rare out-of-line paths
+// take no references into the hot loop's registers.
+struct WarpState {
+  int count;       // entries in the warp's buffer
+  float theta;     // the warp's current threshold
+  int overflow;    // ties at the threshold no longer fit
+};
+
 // Appends the lanes' candidates (one per lane at most) to the warp buffer,
 // compacting first when the ballot would not fit.
-__device__ __forceinline__ void warp_push(bool pred, float v, int id, float* wv, int* wi,
-                                         int& count, int K, float& theta_w, bool& tie_overflow) {
+__device__ __forceinline__ void warp_push(bool pred, float v, int id, float* wv, int* wi, int K,
+                                         WarpState* ws) {
   unsigned b = __ballot_sync(0xffffffffu, pred);
   if (b == 0u) return;
+  int count = ws->count;
   if (count + __popc(b) > TW_WCAP) {
-    if (tie_overflow) return;  // row already goes to the fix-up path
-    count = warp_compact(wv, wi, count, K, theta_w, tie_overflow);
-    pred = pred && v >= theta_w;
+    if (ws->overflow) return;  // row already goes to the fix-up path
+    float th = ws->theta;
+    bool ovf = false;
+    count = warp_compact(wv, wi, count, K, th, ovf);
+    pred = pred && v >= th;
     b = __ballot_sync(0xffffffffu, pred);
-    if (tie_overflow || count + __popc(b) > TW_WCAP) {
-      tie_overflow = true;
-      return;
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+      ws->theta = th;
+      ws->count = count;
+      if (ovf || count + __popc(b) > TW_WCAP) ws->overflow = 1;
     }
+    __syncwarp();
+    if (ws->overflow) return;
   }
   const int lane = threadIdx.x & 31;
   if (pred) {
@@ -134,13 +149,27 @@ __device__ __forceinline__ void warp_push(bool pred, float v, int id, float* wv,
     wv[slot] = v;
     wi[slot] = id;
   }
-  count += __popc(b);
+  __syncwarp();
+  if (lane == 0) ws->count = count + __popc(b);
+  __syncwarp();
+}
+
+// Rare path of the stream loop: append the candidates among one float4 per lane.
+__device__ __noinline__ void warp_push4(bool valid, float v0, float v1, float v2, float v3, int col,
+                                        float* wv, int* wi, int K, WarpState* ws) {
+  const float vv[4] = {v0, v1, v2, v3};
+#pragma unroll 1
+  for (int e = 0; e < 4; ++e) {
+    const float th = ws->theta;
+    const bool c = valid && vv[e] >= th && vv[e] < INFINITY;
+    warp_push(c, canon(vv[e]), col + e, wv, wi, K, ws);
+  }
 }
 
 // Finishing stage by one warp for m <= 64 candidates (TokenSampler.cs:95-132).
 // `wsm` holds 128 floats of shared memory. Only warp 0 calls.
-__device__ void finish_row_warp(const SampleArgs& a, int row, const float* cv, const int* cid,
-                                int m, float* wsm) {
+__device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const float* cv,
+                                            const int* cid, int m, float* wsm) {
   const int lane = threadIdx.x & 31;
   uint64_t k[2];
 #pragma unroll
@@ -256,7 +285,7 @@ __device__ void finish_row_warp(const SampleArgs& a, int row, const float* cv, c
 }
 
 template <bool kCounts>
-__global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* ring = reinterpret_cast<float*>(smem);                          // [W][NST][CH]
   float* wvall = ring + TW_RING_FLOATS;                                  // [W][WCAP]
@@ -274,6 +303,7 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
   __shared__ int s_wn[TW_WARPS];
   __shared__ int s_sh[2];
   __shared__ float s_theta0;
+  __shared__ WarpState s_ws[TW_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
@@ -371,10 +401,14 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
         TW_WARPS * TW_CH, K, hist, s_sh);
     if (tid == 0) s_theta0 = key == 0u ? -INFINITY : kval(key);
   }
+  WarpState* ws = &s_ws[warp];
+  if (lane == 0) {
+    ws->count = 0;
+    ws->theta = s_theta0;
+    ws->overflow = 0;
+  }
   __syncthreads();
   float theta_w = s_theta0;
-  int count = 0;
-  bool tie_ovf = false;
 
   // head/tail scalars (<= 6) go to warp 0's buffer
   if (warp == 0 && hist_ok) {
@@ -390,7 +424,8 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
         v = -INFINITY;
       }
     }
-    warp_push(act && v >= theta_w, canon(v), col, wv, wi, count, K, theta_w, tie_ovf);
+    warp_push(act && v >= theta_w, canon(v), col, wv, wi, K, ws);
+    theta_w = ws->theta;
   }
 
   // ---- 2. stream ------------------------------------------------------------
@@ -408,7 +443,7 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
           break;
         }
       }
-#pragma unroll
+#pragma unroll 1
       for (int m4 = 0; m4 < TW_CH4 / 32; ++m4) {
         const int q = lane + 32 * m4;
         const bool valid = q < (len >> 2);
@@ -437,11 +472,8 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
           any = vv[0] >= theta_w || vv[1] >= theta_w || vv[2] >= theta_w || vv[3] >= theta_w;
         }
         if (__any_sync(0xffffffffu, any)) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const bool c = valid && vv[e] >= theta_w && vv[e] < INFINITY;
-            warp_push(c, canon(vv[e]), col + e, wv, wi, count, K, theta_w, tie_ovf);
-          }
+          warp_push4(valid, vv[0], vv[1], vv[2], vv[3], col, wv, wi, K, ws);
+          theta_w = ws->theta;
         }
       }
       __syncwarp();
@@ -459,7 +491,9 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(SampleArgs a) 
       (void)mbar_wait_bounded(&mybars[j % TW_NST], (uint32_t)((j / TW_NST) & 1));
   }
   // final per-warp cut to the top K (+ ties)
-  if (count > K) count = warp_compact(wv, wi, count, K, theta_w, tie_ovf);
+  int count = ws->count;
+  bool tie_ovf = ws->overflow != 0;
+  if (!tie_ovf && count > K) count = warp_compact(wv, wi, count, K, theta_w, tie_ovf);
   if (tie_ovf && lane == 0) s_overflow = 1;
   if (lane == 0) s_wn[warp] = count;
   __syncthreads();
