@@ -112,58 +112,45 @@ __device__ __noinline__ int warp_compact(float* wv, int* wi, int count, int K, f
   return keep;
 }
 
-// Per-warp stream state, kept in shared memory so the rare out-of-line paths
-// take no references into the hot loop's registers.
-struct WarpState {
-  int count;       // entries in the warp's buffer
-  float theta;     // the warp's current threshold
-  int overflow;    // ties at the threshold no longer fit
+struct Compacted {
+  int count;    // entries kept (the top K plus ties, a sorted prefix)
+  float theta;  // the warp's new threshold: the K-th value
+  int overflow; // ties leave no room for another ballot of 32
 };
 
-// Appends the lanes' candidates (one per lane at most) to the warp buffer,
-// compacting first when the ballot would not fit.
-__device__ __forceinline__ void warp_push(bool pred, float v, int id, float* wv, int* wi, int K,
-                                         WarpState* ws) {
-  unsigned b = __ballot_sync(0xffffffffu, pred);
-  if (b == 0u) return;
-  int count = ws->count;
-  if (count + __popc(b) > TW_WCAP) {
-    if (ws->overflow) return;  // row already goes to the fix-up path
-    float th = ws->theta;
-    bool ovf = false;
-    count = warp_compact(wv, wi, count, K, th, ovf);
-    pred = pred && v >= th;
-    b = __ballot_sync(0xffffffffu, pred);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) {
-      ws->theta = th;
-      ws->count = count;
-      if (ovf || count + __popc(b) > TW_WCAP) ws->overflow = 1;
-    }
-    __syncwarp();
-    if (ws->overflow) return;
-  }
-  const int lane = threadIdx.x & 31;
-  if (pred) {
-    const int slot = count + __popc(b & ((1u << lane) - 1u));
-    wv[slot] = v;
-    wi[slot] = id;
-  }
-  __syncwarp();
-  if (lane == 0) ws->count = count + __popc(b);
-  __syncwarp();
+// Out of line: the compaction runs a few times per warp and row, and keeping
+// its sorting network out of the stream loop keeps that loop small.
+__device__ __noinline__ Compacted warp_compact_nl(float* wv, int* wi, int count, int K) {
+  float th = 0.0f;
+  bool ovf = false;
+  const int n = warp_compact(wv, wi, count, K, th, ovf);
+  return {n, th, ovf ? 1 : 0};
 }
 
-// Rare path of the stream loop: append the candidates among one float4 per lane.
-__device__ __noinline__ void warp_push4(bool valid, float v0, float v1, float v2, float v3, int col,
-                                        float* wv, int* wi, int K, WarpState* ws) {
-  const float vv[4] = {v0, v1, v2, v3};
-#pragma unroll 1
-  for (int e = 0; e < 4; ++e) {
-    const float th = ws->theta;
-    const bool c = valid && vv[e] >= th && vv[e] < INFINITY;
-    warp_push(c, canon(vv[e]), col + e, wv, wi, K, ws);
+// Appends the lanes' candidate (value c_v at column c_id when `c`) to the warp
+// buffer; count/theta/overflow are warp-uniform registers of the caller.
+__device__ __forceinline__ void warp_append_reg(bool c, float c_v, int c_id, float* wv, int* wi,
+                                               int K, int& count, float& theta, bool& ovf) {
+  unsigned b = __ballot_sync(0xffffffffu, c);
+  if (b == 0u) return;
+  if (count + __popc(b) > TW_WCAP) {
+    if (!ovf) {
+      const Compacted r = warp_compact_nl(wv, wi, count, K);
+      count = r.count;
+      theta = r.theta;
+      ovf = r.overflow != 0;
+      c = c && c_v >= theta;
+      b = __ballot_sync(0xffffffffu, c);
+      if (count + __popc(b) > TW_WCAP) ovf = true;
+    }
+    if (ovf) return;  // the row is redone by the fix-up kernel
   }
+  if (c) {
+    const int slot = count + __popc(b & ((1u << (threadIdx.x & 31)) - 1u));
+    wv[slot] = c_v;
+    wi[slot] = c_id;
+  }
+  count += __popc(b);
 }
 
 // Finishing stage by one warp for m <= 64 candidates (TokenSampler.cs:95-132).
@@ -303,7 +290,6 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
   __shared__ int s_wn[TW_WARPS];
   __shared__ int s_sh[2];
   __shared__ float s_theta0;
-  __shared__ WarpState s_ws[TW_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
@@ -386,6 +372,9 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
           s_nonfinite = 1;
         q4[q] = x;
       }
+      // these generic-proxy writes must be ordered before the TMA copy that
+      // later refills this stage: every writing thread fences
+      fence_proxy_async();
     }
   }
   if (lane == 0) s_wn[warp] = first_len;
@@ -401,14 +390,9 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
         TW_WARPS * TW_CH, K, hist, s_sh);
     if (tid == 0) s_theta0 = key == 0u ? -INFINITY : kval(key);
   }
-  WarpState* ws = &s_ws[warp];
-  if (lane == 0) {
-    ws->count = 0;
-    ws->theta = s_theta0;
-    ws->overflow = 0;
-  }
-  __syncthreads();
   float theta_w = s_theta0;
+  int count = 0;
+  bool tie_ovf = false;
 
   // head/tail scalars (<= 6) go to warp 0's buffer
   if (warp == 0 && hist_ok) {
@@ -424,8 +408,7 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
         v = -INFINITY;
       }
     }
-    warp_push(act && v >= theta_w, canon(v), col, wv, wi, K, ws);
-    theta_w = ws->theta;
+    warp_append_reg(act && v >= theta_w, canon(v), col, wv, wi, K, count, theta_w, tie_ovf);
   }
 
   // ---- 2. stream ------------------------------------------------------------
@@ -472,8 +455,10 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
           any = vv[0] >= theta_w || vv[1] >= theta_w || vv[2] >= theta_w || vv[3] >= theta_w;
         }
         if (__any_sync(0xffffffffu, any)) {
-          warp_push4(valid, vv[0], vv[1], vv[2], vv[3], col, wv, wi, K, ws);
-          theta_w = ws->theta;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            warp_append_reg(valid && vv[e] >= theta_w && vv[e] < INFINITY, canon(vv[e]), col + e,
+                            wv, wi, K, count, theta_w, tie_ovf);
         }
       }
       __syncwarp();
@@ -491,9 +476,11 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
       (void)mbar_wait_bounded(&mybars[j % TW_NST], (uint32_t)((j / TW_NST) & 1));
   }
   // final per-warp cut to the top K (+ ties)
-  int count = ws->count;
-  bool tie_ovf = ws->overflow != 0;
-  if (!tie_ovf && count > K) count = warp_compact(wv, wi, count, K, theta_w, tie_ovf);
+  if (!tie_ovf && count > K) {
+    const Compacted r = warp_compact_nl(wv, wi, count, K);
+    count = r.count;
+    tie_ovf = r.overflow != 0;
+  }
   if (tie_ovf && lane == 0) s_overflow = 1;
   if (lane == 0) s_wn[warp] = count;
   __syncthreads();

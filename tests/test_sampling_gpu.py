@@ -24,7 +24,9 @@ def full_check(gpu_sampler, oracle, wl, probs=True, label=""):
     ot, of, op = run_oracle(oracle, wl, oracle.EXP_CR, want_probs=probs)
     assert_exact(gt, gf, ot, of, label)
     if probs:
-        assert np.array_equal(gp, op), label
+        bad = np.argwhere(gp != op)
+        assert bad.size == 0, (label, len(bad), [(int(r), int(c), float(gp[r, c]), float(op[r, c]))
+                                                 for r, c in bad[:6]])
     rt, rf, rp = run_oracle(oracle, wl, oracle.EXP_GLIBC, want_probs=probs)
     rep = parity_report(gt, gf, rt, rf)
     assert rep["differ_unflagged"] == 0, (label, rep)
