@@ -249,14 +249,17 @@ __device__ __forceinline__ int next_pow2(int n) {
 // to 0 under fkey, and callers replace NaNs). Returns 0 (keep everything) when
 // fewer than k elements exist. 8 bits per pass; `hist` = 256 words of smem,
 // `sh` = 2 ints of smem. Ends with a __syncthreads().
+// With passes < 4 the result is the k-th largest key with its low bits
+// cleared: a lower bound of it (what a threshold filter needs).
 template <typename GetKey>
-__device__ uint32_t cta_kth_largest(GetKey getKey, int n, int k, uint32_t* hist, int* sh) {
+__device__ uint32_t cta_kth_largest(GetKey getKey, int n, int k, uint32_t* hist, int* sh,
+                                    int passes = 4) {
   if (k <= 0) return 0u;
   uint32_t prefix = 0u, mask = 0u;
   int krem = k;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
+  for (int pass = 0; pass < passes; ++pass) {
     const int shift = 24 - 8 * pass;
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();

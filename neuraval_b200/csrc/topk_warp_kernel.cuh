@@ -76,6 +76,9 @@ __device__ __forceinline__ void warp_sort128_desc(uint64_t (&k)[4]) {
 __device__ __noinline__ int warp_compact(float* wv, int* wi, int count, int K, float& theta_w,
                                          bool& tie_overflow) {
   const int lane = threadIdx.x & 31;
+  // entries were appended by other lanes: make their shared-memory writes
+  // visible (ballot/shuffle synchronise execution, not memory)
+  __syncwarp();
   uint64_t k[4];
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -349,6 +352,12 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
   auto val = [&](float l, int col) -> float {
     return __fmul_rn(adjust(P, l, col), scale);
   };
+  // Penalties active on this row, and whether they can only lower a value
+  // (repetition >= 1 divides positives and multiplies non-positives by >= 1;
+  // non-negative frequency/presence subtract): then raw*scale >= theta is a
+  // superset test and exact values are needed only for candidates.
+  const bool pen_active = P.rep || P.cnt;
+  const bool pen_lowers = !(P.rep && P.pen < 1.0f) && !(P.cnt && (P.freq < 0.0f || P.pres < 0.0f));
 
   // ---- 1. first chunk of every warp -> theta0 ------------------------------
   int consumed = 0;
@@ -387,9 +396,12 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
           const float v = ring[w * TW_NST * TW_CH + r];
           return (v < INFINITY) ? fkey(canon(v)) : 0u;
         },
-        TW_WARPS * TW_CH, K, hist, s_sh);
+        TW_WARPS * TW_CH, K, hist, s_sh, 2);
+    // two radix passes: the sample's K-th largest key with its low 16 bits
+    // cleared, still a lower bound of the segment's K-th largest value
     if (tid == 0) s_theta0 = key == 0u ? -INFINITY : kval(key);
   }
+  __syncthreads();
   float theta_w = s_theta0;
   int count = 0;
   bool tie_ovf = false;
@@ -432,9 +444,12 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
         const bool valid = q < (len >> 2);
         const int col = base + 4 * q;
         float vv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
         bool any = false;
+        // `exact`: vv already holds the penalised values
+        bool exact = (j == 0) || !pen_active;
         if (valid) {
-          const float4 x = q4[q];
+          x = q4[q];
           if (j == 0) {  // already penalised and scaled in place
             vv[0] = x.x; vv[1] = x.y; vv[2] = x.z; vv[3] = x.w;
           } else {
@@ -442,19 +457,32 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
             vv[1] = __fmul_rn(x.y, scale);
             vv[2] = __fmul_rn(x.z, scale);
             vv[3] = __fmul_rn(x.w, scale);
-            if ((P.rep || P.cnt) && penalty_bits4(P, col) != 0u) {
+            if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
+                !(vv[3] < INFINITY))
+              s_nonfinite = 1;
+            if (pen_active && !pen_lowers && penalty_bits4(P, col) != 0u) {
+              // a penalty that can raise a value: exact values up front
               vv[0] = val(x.x, col);
               vv[1] = val(x.y, col + 1);
               vv[2] = val(x.z, col + 2);
               vv[3] = val(x.w, col + 3);
+              if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
+                  !(vv[3] < INFINITY))
+                s_nonfinite = 1;
+              exact = true;
             }
-            if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
-                !(vv[3] < INFINITY))
-              s_nonfinite = 1;
           }
+          // penalties that only lower values: raw*scale >= theta is a superset test
           any = vv[0] >= theta_w || vv[1] >= theta_w || vv[2] >= theta_w || vv[3] >= theta_w;
         }
         if (__any_sync(0xffffffffu, any)) {
+          if (!exact && any) {
+            // exact penalised values for this lane's four (only near the threshold)
+            vv[0] = val(x.x, col);
+            vv[1] = val(x.y, col + 1);
+            vv[2] = val(x.z, col + 2);
+            vv[3] = val(x.w, col + 3);
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             warp_append_reg(valid && vv[e] >= theta_w && vv[e] < INFINITY, canon(vv[e]), col + e,
@@ -475,12 +503,7 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
     for (int j = consumed; j < issued; ++j)
       (void)mbar_wait_bounded(&mybars[j % TW_NST], (uint32_t)((j / TW_NST) & 1));
   }
-  // final per-warp cut to the top K (+ ties)
-  if (!tie_ovf && count > K) {
-    const Compacted r = warp_compact_nl(wv, wi, count, K);
-    count = r.count;
-    tie_ovf = r.overflow != 0;
-  }
+  // (no final per-warp cut: the segment select below reads the buffers whole)
   if (tie_ovf && lane == 0) s_overflow = 1;
   if (lane == 0) s_wn[warp] = count;
   __syncthreads();
