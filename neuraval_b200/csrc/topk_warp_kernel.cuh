@@ -399,7 +399,8 @@ __global__ void __launch_bounds__(TW_THREADS, 2) topk_warp_kernel(const __grid_c
         TW_WARPS * TW_CH, K, hist, s_sh, 2);
     // two radix passes: the sample's K-th largest key with its low 16 bits
     // cleared, still a lower bound of the segment's K-th largest value
-    if (tid == 0) s_theta0 = key == 0u ? -INFINITY : kval(key);
+    // keys at or below the key of -inf decode to NaN patterns: accept all
+    if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
   }
   __syncthreads();
   float theta_w = s_theta0;
