@@ -23,6 +23,7 @@ NVCC_FLAGS = [
     # every float expression that decides a token must round exactly as written
     "-fmad=false",
     "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-I", os.path.join(ROOT, "include"),
 ]
 
 

@@ -7,7 +7,7 @@
 // global recursive mutex, a sampler handle carries its own lock, and the
 // host-array entry point reuses handle-owned device buffers instead of
 // allocating per call.
-#include "../../include/navsampler.h"
+#include "navsampler.h"
 
 #include <atomic>
 #include <cstdlib>
@@ -18,7 +18,7 @@
 #include "logits_ops.cuh"
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
-#include "topk_warp_kernel.cuh"
+#include "topk_ldg_kernel.cuh"
 
 namespace {
 
@@ -133,8 +133,8 @@ static bool raise_smem_limits(int limit) {
   };
   set((const void*)nvs::topk_kernel<true>);
   set((const void*)nvs::topk_kernel<false>);
-  set((const void*)nvs::topk_warp_kernel<true>);
-  set((const void*)nvs::topk_warp_kernel<false>);
+  set((const void*)nvs::topk_ldg_kernel<true>);
+  set((const void*)nvs::topk_ldg_kernel<false>);
   set((const void*)nvs::greedy_kernel<true>);
   set((const void*)nvs::greedy_kernel<false>);
   set((const void*)nvs::fullvocab_kernel<true>);
@@ -301,18 +301,19 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   }
 
   const int K = prm->top_k < V ? prm->top_k : V;
-  if (K < V && K <= nvs::TW_KMAX) {
+  if (K < V && K <= nvs::TL_KMAX) {
     int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);
     S = (V + a.seg_len - 1) / a.seg_len;
     if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
     a.bm_words = (a.seg_len + 31) / 32 + 1;
-    const size_t smem = nvs::tw_smem_bytes(a.bm_words, a.h_cap);
+    const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
     if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
     dim3 grid(S, rows);
-    if (counts) nvs::topk_warp_kernel<true><<<grid, nvs::TW_THREADS, smem, stream>>>(a);
-    else nvs::topk_warp_kernel<false><<<grid, nvs::TW_THREADS, smem, stream>>>(a);
+    if (counts) nvs::topk_ldg_kernel<true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    else nvs::topk_ldg_kernel<false><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
     if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    // rows whose ties overflowed the candidate buffers (normally none)
     return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, true, 8);
   }
   if (K < V && K <= nvs::TK_KMAX) {

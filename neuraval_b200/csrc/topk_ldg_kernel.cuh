@@ -1,0 +1,407 @@
+// Streaming top-k sampling kernel for k <= 64 (sm_100a), 128-bit loads.
+//
+// Same semantics as topk_kernel (TokenSampler.cs:54-135); the schedule is
+// built for HBM throughput:
+//  - every thread streams its float4s with four independent 128-bit loads in
+//    flight (evict-first), so the row is read exactly once at full bandwidth
+//    with no shared-memory staging and no barriers in the loop;
+//  - the first batch (4 float4 per thread, 8192 values per CTA) is also the
+//    sample: a two-pass CTA radix select over it, with per-warp aggregation of
+//    equal histogram bins, gives theta0, a lower bound of the segment's K-th
+//    largest value;
+//  - values >= the warp's threshold go to a per-warp candidate buffer (ballot
+//    + popc); a full buffer is sorted in registers and cut to its top K plus
+//    ties, which raises that warp's threshold;
+//  - one CTA select over the warp buffers gives the segment's K-th largest;
+//    one warp (or the CTA, for > 64 candidates) runs the exact finish.
+// Penalties that can only lower a value (repetition >= 1, frequency and
+// presence >= 0) are applied to candidates only: raw*scale >= theta is a
+// superset test.
+#pragma once
+
+#include "sampler_device.cuh"
+#include "topk_kernels.cuh"
+#include "warp_select.cuh"
+
+namespace nvs {
+
+constexpr int TL_THREADS = 512;
+constexpr int TL_WARPS = TL_THREADS / 32;
+constexpr int TL_UNROLL = 4;                       // float4 loads in flight per thread
+constexpr int TL_STEP = TL_THREADS * TL_UNROLL;    // float4 per CTA step
+constexpr int TL_KMAX = 64;
+
+inline size_t tl_smem_bytes(int bm_words, int h_cap) {
+  return (size_t)TL_WARPS * TW_WCAP * 8      // warp buffers
+         + (size_t)TK_CAPB * 8               // compact candidate list
+         + (size_t)32768                     // finish / merge work area
+         + 256 * 4                           // radix histogram
+         + (size_t)bm_words * 4 + (size_t)h_cap * 4;
+}
+
+// Histogram add with equal bins of a warp combined into one atomic.
+__device__ __forceinline__ void hist_add_aggregated(uint32_t* hist, bool pred, uint32_t bin) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t tag = pred ? bin : (0x10000u | (uint32_t)lane);  // unique when unused
+  const unsigned peers = __match_any_sync(0xffffffffu, tag);
+  if (pred && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+}
+
+// k-th largest key (with low bits cleared after `passes` < 4 passes) among the
+// N keys each thread holds in registers (key 0 = not an element). All threads
+// call. Returns 0 when fewer than k elements exist. Ends with __syncthreads().
+template <int N>
+__device__ uint32_t cta_kth_largest_regs(const uint32_t (&keys)[N], int k, int passes,
+                                         uint32_t* hist, int* sh) {
+  uint32_t prefix = 0u, mask = 0u;
+  int krem = k;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll 1
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const bool in = keys[j] != 0u && (keys[j] & mask) == prefix;
+      hist_add_aggregated(hist, in, (keys[j] >> shift) & 255u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int c[8];
+      int sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = (int)hist[255 - 8 * lane - j];
+        sum += c[j];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int total = __shfl_sync(0xffffffffu, incl, 31);
+      if (lane == 0 && total < krem) {
+        sh[0] = -1;
+        sh[1] = 0;
+      }
+      const int excl = incl - sum;
+      if (total >= krem && excl < krem && krem <= incl) {
+        int run = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (run + c[j] >= krem) {
+            sh[0] = 255 - 8 * lane - j;
+            sh[1] = run;
+            break;
+          }
+          run += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    const int digit = sh[0];
+    if (digit < 0) {
+      __syncthreads();
+      return 0u;
+    }
+    krem -= sh[1];
+    prefix |= (uint32_t)digit << shift;
+    mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+template <bool kCounts>
+__global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* wvall = reinterpret_cast<float*>(smem);                           // [W][WCAP]
+  int* wiall = reinterpret_cast<int*>(wvall + TL_WARPS * TW_WCAP);         // [W][WCAP]
+  float* cv = reinterpret_cast<float*>(wiall + TL_WARPS * TW_WCAP);        // [CAPB]
+  int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                         // [CAPB]
+  unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);   // 32 KiB
+  uint32_t* hist = reinterpret_cast<uint32_t*>(work + 32768);              // [256]
+  uint32_t* bitmap = hist + 256;
+  int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
+
+  __shared__ int s_hn, s_nonfinite, s_overflow, s_count, s_last, s_ovf, s_tot;
+  __shared__ int s_wn[TL_WARPS];
+  __shared__ int s_sh[2];
+  __shared__ float s_theta0;
+  __shared__ uint32_t s_state;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
+  const int V = a.V;
+  const int K = min(a.p.top_k, V);
+  const int c0 = split * a.seg_len;
+  const int c1 = min(V, c0 + a.seg_len);
+  const float* lrow = a.logits + (size_t)row * V;
+  const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
+
+  Penalty P;
+  const bool hist_ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
+  const bool pen_active = P.rep || P.cnt;
+  const bool pen_lowers = !(P.rep && P.pen < 1.0f) && !(P.cnt && (P.freq < 0.0f || P.pres < 0.0f));
+  auto val = [&](float l, int col) -> float { return __fmul_rn(adjust(P, l, col), scale); };
+
+  if (tid == 0) {
+    s_nonfinite = 0;
+    s_overflow = 0;
+  }
+  if (a.probs) {
+    float* prow = a.probs + (size_t)row * V;
+    for (int c = c0 + tid; c < c1; c += TL_THREADS) prow[c] = 0.0f;
+  }
+  __syncthreads();
+
+  // 16-byte aligned body [a0,a1) as float4; <=3 head and <=3 tail scalars
+  const int head = (int)(((16u - ((uint32_t)(uintptr_t)(lrow + c0) & 15u)) & 15u) >> 2);
+  const int a0 = min(c0 + head, c1);
+  const int a1 = a0 + ((c1 - a0) & ~3);
+  const int n4 = (a1 - a0) >> 2;
+  const float4* body = reinterpret_cast<const float4*>(lrow + a0);
+
+  float* wv = wvall + warp * TW_WCAP;
+  int* wi = wiall + warp * TW_WCAP;
+  int count = 0;
+  bool tie_ovf = false;
+  bool nonfinite = false;
+
+  // ---- first batch: load, exact values, sample select ----------------------
+  float4 x[TL_UNROLL];
+  uint32_t skeys[TL_UNROLL * 4];
+#pragma unroll
+  for (int u = 0; u < TL_UNROLL; ++u) {
+    const int q = tid + u * TL_THREADS;
+    x[u] = (hist_ok && q < n4) ? __ldcs(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < TL_UNROLL; ++u) {
+    const int q = tid + u * TL_THREADS;
+    const bool valid = hist_ok && q < n4;
+    const int col = a0 + 4 * q;
+    float e[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v = valid ? val(e[j], col + j) : -INFINITY;
+      if (!(v < INFINITY)) {
+        nonfinite = nonfinite || valid;
+        v = -INFINITY;
+      }
+      e[j] = v;
+      skeys[u * 4 + j] = valid ? fkey(canon(v)) : 0u;
+    }
+    x[u] = make_float4(e[0], e[1], e[2], e[3]);  // x now holds exact values
+  }
+  {
+    const uint32_t key = cta_kth_largest_regs(skeys, K, 2, hist, s_sh);
+    // keys at or below the key of -inf decode to NaN patterns: accept all
+    if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
+  }
+  __syncthreads();
+  float theta_w = s_theta0;
+
+  // head/tail scalars (<= 6) go to warp 0's buffer
+  if (warp == 0 && hist_ok) {
+    const int nh = a0 - c0, nt = c1 - a1;
+    const bool act = lane < nh + nt;
+    float v = -INFINITY;
+    int col = 0;
+    if (act) {
+      col = lane < nh ? c0 + lane : a1 + (lane - nh);
+      v = val(lrow[col], col);
+      if (!(v < INFINITY)) {
+        nonfinite = true;
+        v = -INFINITY;
+      }
+    }
+    warp_append_reg(act && v >= theta_w, canon(v), col, wv, wi, K, count, theta_w, tie_ovf);
+  }
+  // candidates of the first batch (exact values already)
+#pragma unroll
+  for (int u = 0; u < TL_UNROLL; ++u) {
+    const int q = tid + u * TL_THREADS;
+    const bool valid = hist_ok && q < n4;
+    const int col = a0 + 4 * q;
+    const bool any = valid && (x[u].x >= theta_w || x[u].y >= theta_w || x[u].z >= theta_w ||
+                               x[u].w >= theta_w);
+    if (__any_sync(0xffffffffu, any)) {
+      const float e[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        warp_append_reg(valid && e[j] >= theta_w, canon(e[j]), col + j, wv, wi, K, count, theta_w,
+                        tie_ovf);
+    }
+  }
+
+  // ---- stream the rest ---------------------------------------------------------
+  if (hist_ok) {
+#pragma unroll 1
+    for (int base = tid + TL_STEP; base - tid < n4; base += TL_STEP) {
+#pragma unroll
+      for (int u = 0; u < TL_UNROLL; ++u) {
+        const int q = base + u * TL_THREADS;
+        x[u] = q < n4 ? __ldcs(body + q) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+#pragma unroll
+      for (int u = 0; u < TL_UNROLL; ++u) {
+        const int q = base + u * TL_THREADS;
+        const bool valid = q < n4;
+        const int col = a0 + 4 * q;
+        float vv[4] = {__fmul_rn(x[u].x, scale), __fmul_rn(x[u].y, scale),
+                       __fmul_rn(x[u].z, scale), __fmul_rn(x[u].w, scale)};
+        if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
+            !(vv[3] < INFINITY))
+          nonfinite = true;
+        bool exact = !pen_active;
+        if (pen_active && !pen_lowers && valid && penalty_bits4(P, col) != 0u) {
+          // a penalty that can raise a value: exact values up front
+          vv[0] = val(x[u].x, col);
+          vv[1] = val(x[u].y, col + 1);
+          vv[2] = val(x[u].z, col + 2);
+          vv[3] = val(x[u].w, col + 3);
+          if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
+              !(vv[3] < INFINITY))
+            nonfinite = true;
+          exact = true;
+        }
+        const bool any = valid && (vv[0] >= theta_w || vv[1] >= theta_w || vv[2] >= theta_w ||
+                                   vv[3] >= theta_w);
+        if (__any_sync(0xffffffffu, any)) {
+          if (any && !exact) {  // exact penalised values near the threshold only
+            vv[0] = val(x[u].x, col);
+            vv[1] = val(x[u].y, col + 1);
+            vv[2] = val(x[u].z, col + 2);
+            vv[3] = val(x[u].w, col + 3);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            warp_append_reg(valid && vv[j] >= theta_w && vv[j] < INFINITY, canon(vv[j]), col + j,
+                            wv, wi, K, count, theta_w, tie_ovf);
+        }
+      }
+    }
+  }
+  if (nonfinite) s_nonfinite = 1;
+  if (tie_ovf && lane == 0) s_overflow = 1;
+  if (lane == 0) s_wn[warp] = count;
+  __syncwarp();
+  __syncthreads();
+
+  // ---- segment threshold over the warp buffers ------------------------------
+  uint32_t state = 0u;
+  if (!hist_ok) state |= FLAG_BAD_HISTORY;
+  if (s_nonfinite) state |= FLAG_NONFINITE;
+  if (s_overflow) state |= RSTATE_OVERFLOW;
+  int m = 0;
+  if (state == 0u) {
+    uint32_t wk[TW_WCAP / 32];
+#pragma unroll
+    for (int r = 0; r < TW_WCAP / 32; ++r) {
+      // thread tid covers entries tid + r*512 of the flattened [W][WCAP] buffers
+      const int i = tid + r * TL_THREADS;
+      const int w = i / TW_WCAP, e = i % TW_WCAP;
+      wk[r] = e < s_wn[w] ? fkey(wvall[i]) : 0u;
+    }
+    const uint32_t key = cta_kth_largest_regs(wk, K, 4, hist, s_sh);
+    if (tid == 0) {
+      s_count = 0;
+      s_ovf = 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < TW_WCAP / 32; ++r) {
+      const int i = tid + r * TL_THREADS;
+      const bool ok = wk[r] != 0u && wk[r] >= key;
+      warp_append(ok, ok ? wvall[i] : 0.f, ok ? wiall[i] : 0, cv, cid, &s_count, &s_ovf);
+    }
+    __syncthreads();
+    m = min(s_count, TK_CAPB);
+    if (s_ovf) state |= RSTATE_OVERFLOW;
+  }
+
+  if (S == 1) {
+    if (state == 0u && m > 0 && m <= 64) {
+      if (warp == 0) finish_row_warp(a, row, cv, cid, m, reinterpret_cast<float*>(work));
+    } else {
+      finish_row(a, row, cv, cid, m, state, work);
+    }
+    return;
+  }
+
+  // ---- multi-CTA rows: publish, the last CTA merges --------------------------
+  const int cta = row * S + split;
+  for (int i = tid; i < m; i += TL_THREADS) {
+    a.s.cand_v[(size_t)cta * TK_CAPB + i] = cv[i];
+    a.s.cand_id[(size_t)cta * TK_CAPB + i] = cid[i];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    a.s.cand_n[cta] = m;
+    if (state) atomicOr(&a.s.rowstate[row], state);
+    __threadfence();
+    const uint32_t t = atomicAdd(&a.s.tickets[row], 1u);
+    s_last = (t == (uint32_t)(S - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* uv = reinterpret_cast<float*>(work);            // union: [0, 8 KiB)
+  int* uid = reinterpret_cast<int*>(uv + TK_CAPB);        //        [8, 16 KiB)
+  if (tid == 0) {
+    s_state = __ldcg(&a.s.rowstate[row]);
+    int tot = 0;
+    for (int sp = 0; sp < S; ++sp) tot += __ldcg(&a.s.cand_n[row * S + sp]);
+    s_tot = tot;
+  }
+  __syncthreads();
+  uint32_t mstate = s_state;
+  const int total = s_tot;
+  if (total > TK_CAPB) mstate |= RSTATE_OVERFLOW;
+  int mm = 0;
+  if (mstate == 0u) {
+    int off = 0;
+    for (int sp = 0; sp < S; ++sp) {
+      const int n = __ldcg(&a.s.cand_n[row * S + sp]);
+      const size_t g = (size_t)(row * S + sp) * TK_CAPB;
+      for (int i = tid; i < n; i += TL_THREADS) {
+        uv[off + i] = __ldcg(&a.s.cand_v[g + i]);
+        uid[off + i] = __ldcg(&a.s.cand_id[g + i]);
+      }
+      off += n;
+    }
+    __syncthreads();
+    const uint32_t key = cta_kth_largest([&](int i) { return fkey(uv[i]); }, total, K, hist, s_sh);
+    if (tid == 0) {
+      s_count = 0;
+      s_ovf = 0;
+    }
+    __syncthreads();
+    for (int i0 = 0; i0 < total; i0 += TL_THREADS) {
+      const int i = i0 + tid;
+      const bool ok = i < total && fkey(uv[i]) >= key;
+      warp_append(ok, ok ? uv[i] : 0.f, ok ? uid[i] : 0, cv, cid, &s_count, &s_ovf);
+    }
+    __syncthreads();
+    if (s_ovf) mstate |= RSTATE_OVERFLOW;
+    mm = min(s_count, TK_CAPB);
+  }
+  __syncthreads();
+  // the union is dead now: the finish reuses the work area
+  if (mstate == 0u && mm > 0 && mm <= 64) {
+    if (warp == 0) finish_row_warp(a, row, cv, cid, mm, reinterpret_cast<float*>(work));
+  } else {
+    finish_row(a, row, cv, cid, mm, mstate, work);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    a.s.rowstate[row] = 0u;
+    a.s.tickets[row] = 0u;
+  }
+}
+
+}  // namespace nvs

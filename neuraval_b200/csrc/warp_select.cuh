@@ -1,0 +1,255 @@
+// Warp-level candidate buffers and the one-warp finishing stage shared by
+// the streaming top-k kernels (sm_100a).
+//
+// A warp keeps the values >= its threshold in a private shared-memory buffer
+// (appends by ballot + popc, no atomics). A full buffer is sorted in registers
+// (bitonic network on 64-bit value/id keys) and cut to its top K plus every
+// value equal to the K-th, which raises the warp's threshold; that cut is a
+// lower bound of the segment's K-th largest value, so no candidate of the
+// final threshold is ever dropped. Ties that fill the buffer mark the row for
+// the full-vocabulary fix-up kernel.
+#pragma once
+
+#include "sampler_device.cuh"
+#include "topk_kernels.cuh"
+
+namespace nvs {
+
+constexpr int TW_WCAP = 128;   // candidate entries per warp buffer
+
+// Warp bitonic sort, descending, of 128 keys held 4 per lane at index r*32+lane.
+__device__ __forceinline__ void warp_sort128_desc(uint64_t (&k)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 128; size <<= 1) {
+#pragma unroll
+    for (int j = size >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int i = r * 32 + lane;
+        const bool down = (i & size) == 0;  // this block sorts descending
+        if (j >= 32) {
+          const int rr = r ^ (j >> 5);
+          if (rr > r) {
+            const uint64_t x = k[r], y = k[rr];
+            const bool sw = down ? (x < y) : (x > y);
+            if (sw) { k[r] = y; k[rr] = x; }
+          }
+        } else {
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, k[r], j);
+          const bool lower = (lane & j) == 0;
+          // lower index keeps the larger key in a descending block
+          const uint64_t mx = k[r] > o ? k[r] : o, mn = k[r] > o ? o : k[r];
+          k[r] = (lower == down) ? mx : mn;
+        }
+      }
+    }
+  }
+}
+
+// Sorts the warp's buffer, keeps the top K values plus every value equal to the
+// K-th (a sorted prefix), and returns the new count; theta_w becomes the K-th
+// value. When the kept prefix would leave no room for another ballot of 32,
+// *tie_overflow is set.
+__device__ __noinline__ int warp_compact(float* wv, int* wi, int count, int K, float& theta_w,
+                                         bool& tie_overflow) {
+  const int lane = threadIdx.x & 31;
+  // entries were appended by other lanes: make their shared-memory writes
+  // visible (ballot/shuffle synchronise execution, not memory)
+  __syncwarp();
+  uint64_t k[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = r * 32 + lane;
+    k[r] = i < count ? cand_key(wv[i], wi[i]) : 0ull;
+  }
+  warp_sort128_desc(k);
+  // key of the K-th entry (index K-1 = r*32+lane)
+  const int rK = (K - 1) >> 5, lK = (K - 1) & 31;
+  uint64_t kk = 0;
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    if (r == rK) kk = __shfl_sync(0xffffffffu, k[r], lK);
+  const uint32_t tkey = (uint32_t)(kk >> 32);
+  int keep = 0;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = r * 32 + lane;
+    const bool kp = i < count && (uint32_t)(k[r] >> 32) >= tkey;
+    keep += __popc(__ballot_sync(0xffffffffu, kp));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = r * 32 + lane;
+    if (i < keep) {
+      wv[i] = cand_val(k[r]);
+      wi[i] = cand_id(k[r]);
+    }
+  }
+  __syncwarp();
+  theta_w = kval(tkey);
+  if (keep > TW_WCAP - 32) tie_overflow = true;
+  return keep;
+}
+
+struct Compacted {
+  int count;    // entries kept (the top K plus ties, a sorted prefix)
+  float theta;  // the warp's new threshold: the K-th value
+  int overflow; // ties leave no room for another ballot of 32
+};
+
+// Out of line: the compaction runs a few times per warp and row, and keeping
+// its sorting network out of the stream loop keeps that loop small.
+__device__ __noinline__ Compacted warp_compact_nl(float* wv, int* wi, int count, int K) {
+  float th = 0.0f;
+  bool ovf = false;
+  const int n = warp_compact(wv, wi, count, K, th, ovf);
+  return {n, th, ovf ? 1 : 0};
+}
+
+// Appends the lanes' candidate (value c_v at column c_id when `c`) to the warp
+// buffer; count/theta/overflow are warp-uniform registers of the caller.
+__device__ __forceinline__ void warp_append_reg(bool c, float c_v, int c_id, float* wv, int* wi,
+                                               int K, int& count, float& theta, bool& ovf) {
+  unsigned b = __ballot_sync(0xffffffffu, c);
+  if (b == 0u) return;
+  if (count + __popc(b) > TW_WCAP) {
+    if (!ovf) {
+      const Compacted r = warp_compact_nl(wv, wi, count, K);
+      count = r.count;
+      theta = r.theta;
+      ovf = r.overflow != 0;
+      c = c && c_v >= theta;
+      b = __ballot_sync(0xffffffffu, c);
+      if (count + __popc(b) > TW_WCAP) ovf = true;
+    }
+    if (ovf) return;  // the row is redone by the fix-up kernel
+  }
+  if (c) {
+    const int slot = count + __popc(b & ((1u << (threadIdx.x & 31)) - 1u));
+    wv[slot] = c_v;
+    wi[slot] = c_id;
+  }
+  count += __popc(b);
+}
+
+// Finishing stage by one warp for m <= 64 candidates (TokenSampler.cs:95-132).
+// `wsm` holds 128 floats of shared memory. Only warp 0 calls.
+__device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const float* cv,
+                                            const int* cid, int m, float* wsm) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = r * 32 + lane;
+    k[r] = i < m ? cand_key(cv[i], cid[i]) : 0ull;
+  }
+  // bitonic sort of 64 keys, descending
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+    for (int j = size >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int i = r * 32 + lane;
+        const bool down = (i & size) == 0;
+        if (j >= 32) {
+          if (r == 0) {
+            const uint64_t x = k[0], y = k[1];
+            const bool sw = down ? (x < y) : (x > y);
+            if (sw) { k[0] = y; k[1] = x; }
+          }
+        } else {
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, k[r], j);
+          const bool lower = (lane & j) == 0;
+          const uint64_t mx = k[r] > o ? k[r] : o, mn = k[r] > o ? o : k[r];
+          k[r] = (lower == down) ? mx : mn;
+        }
+      }
+    }
+  }
+  const float vmax = cand_val(__shfl_sync(0xffffffffu, k[0], 0));
+  float* w = wsm;        // [64]
+  float* S = wsm + 64;   // [64]
+  if (!(vmax > -INFINITY)) {
+    if (lane == 0) {
+      a.tokens[row] = -1;
+      if (a.flags) a.flags[row] = FLAG_NONFINITE;
+    }
+    return;
+  }
+  bool slow = false;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = r * 32 + lane;
+    if (i < m) w[i] = exp_cr(__fsub_rn(cand_val(k[r]), vmax), slow);
+  }
+  const bool any_slow = __any_sync(0xffffffffu, slow);
+  __syncwarp();
+  int cutoff = m, sel = 0;
+  float retained = 0.0f;
+  if (lane == 0) {
+    float total = 0.0f;
+    for (int i = 0; i < m; ++i) {
+      total = __fadd_rn(total, w[i]);
+      S[i] = total;
+    }
+    float target = 0.0f;
+    if (a.p.top_p < 1.0f) {
+      target = __fmul_rn(total, a.p.top_p);
+      for (int i = 0; i < m; ++i)
+        if (S[i] >= target) { cutoff = i + 1; break; }
+    }
+    retained = S[cutoff - 1];
+    const float sample = __fmul_rn(a.uniforms[row], retained);
+    sel = cutoff - 1;
+    for (int i = 0; i < cutoff; ++i)
+      if (sample <= S[i]) { sel = i; break; }
+    uint32_t f = any_slow ? FLAG_EXP_SLOW : 0u;
+    const double tol = 1e-6 * (double)retained;
+    if (fabs((double)sample - (double)S[sel]) <= tol ||
+        (sel >= 1 && fabs((double)sample - (double)S[sel - 1]) <= tol))
+      f |= FLAG_DRAW_BOUNDARY;
+    if (a.p.top_p < 1.0f) {
+      const double tt = 1e-6 * (double)target;
+      if (fabs((double)S[cutoff - 1] - (double)target) <= tt ||
+          (cutoff >= 2 && fabs((double)S[cutoff - 2] - (double)target) <= tt))
+        f |= FLAG_CUTOFF_BOUNDARY;
+    }
+    if (a.flags) a.flags[row] = f;
+  }
+  cutoff = __shfl_sync(0xffffffffu, cutoff, 0);
+  sel = __shfl_sync(0xffffffffu, sel, 0);
+  retained = __shfl_sync(0xffffffffu, retained, 0);
+  // token and the tie flag from the sorted keys
+  const int rs = sel >> 5, ls = sel & 31;
+  uint64_t ksel = 0, kprev = 0, knext = 0;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint64_t t0 = __shfl_sync(0xffffffffu, k[r], ls);
+    if (r == rs) ksel = t0;
+    const int ip = sel - 1, in = sel + 1;
+    const uint64_t tp = __shfl_sync(0xffffffffu, k[r], ip & 31);
+    const uint64_t tn = __shfl_sync(0xffffffffu, k[r], in & 31);
+    if (ip >= 0 && r == (ip >> 5)) kprev = tp;
+    if (r == (in >> 5)) knext = tn;
+  }
+  if (lane == 0) {
+    const uint32_t ks = (uint32_t)(ksel >> 32);
+    const bool tie = (sel > 0 && (uint32_t)(kprev >> 32) == ks) ||
+                     (sel + 1 < m && (uint32_t)(knext >> 32) == ks);
+    a.tokens[row] = cand_id(ksel);
+    if (tie && a.flags) a.flags[row] |= FLAG_TIE_AT_DRAW;
+  }
+  if (a.probs) {
+    float* prow = a.probs + (size_t)row * a.V;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = r * 32 + lane;
+      if (i < cutoff) prow[cand_id(k[r])] = __fdiv_rn(w[i], retained);
+    }
+  }
+}
+
+}  // namespace nvs
