@@ -3,20 +3,22 @@
 // Same semantics as topk_kernel (TokenSampler.cs:54-135); the schedule is
 // built for HBM throughput:
 //  - every thread streams its float4s with four independent 128-bit loads in
-//    flight (evict-first), so the row is read exactly once at full bandwidth
-//    with no shared-memory staging and no barriers in the loop;
-//  - the first batch (4 float4 per thread, 8192 values per CTA) is also the
-//    sample: a two-pass CTA radix select over it, with per-warp aggregation of
-//    equal histogram bins, gives theta0, a lower bound of the segment's K-th
-//    largest value;
-//  - values >= the warp's threshold go to a per-warp candidate buffer (ballot
-//    + popc); a full buffer is sorted in registers and cut to its top K plus
-//    ties, which raises that warp's threshold;
+//    flight (evict-first), so the row is read once with no shared-memory
+//    staging and no barrier in the loop. Per value the loop does one multiply,
+//    one NaN/+inf test and one threshold test; one vote per step of 16 values
+//    decides whether the out-of-line candidate path runs at all;
+//  - the first step is also the sample: exact (penalised) values, each
+//    thread's maximum, and the K-th largest of those 512 maxima -- distinct
+//    elements of the segment, so a lower bound of its K-th largest value;
+//  - candidates go to per-warp buffers (ballot + popc); a full buffer is
+//    sorted in registers and cut to its top K plus ties, raising that warp's
+//    threshold;
 //  - one CTA select over the warp buffers gives the segment's K-th largest;
-//    one warp (or the CTA, for > 64 candidates) runs the exact finish.
+//    one warp (or the CTA, above 64 candidates) runs the exact finish.
 // Penalties that can only lower a value (repetition >= 1, frequency and
 // presence >= 0) are applied to candidates only: raw*scale >= theta is a
-// superset test.
+// superset test. Other penalties take the exact path for every float4 that
+// holds a penalised id.
 #pragma once
 
 #include "sampler_device.cuh"
@@ -30,41 +32,42 @@ constexpr int TL_WARPS = TL_THREADS / 32;
 constexpr int TL_UNROLL = 4;                       // float4 loads in flight per thread
 constexpr int TL_STEP = TL_THREADS * TL_UNROLL;    // float4 per CTA step
 constexpr int TL_KMAX = 64;
+constexpr int TL_WORK = 32768;                     // finish / merge / histogram work area
 
 inline size_t tl_smem_bytes(int bm_words, int h_cap) {
   return (size_t)TL_WARPS * TW_WCAP * 8      // warp buffers
          + (size_t)TK_CAPB * 8               // compact candidate list
-         + (size_t)32768                     // finish / merge work area
+         + (size_t)TL_WORK                   // finish / merge work, per-warp histograms
          + 256 * 4                           // radix histogram
          + (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
 
-// Histogram add with equal bins of a warp combined into one atomic.
-__device__ __forceinline__ void hist_add_aggregated(uint32_t* hist, bool pred, uint32_t bin) {
-  const int lane = threadIdx.x & 31;
-  const uint32_t tag = pred ? bin : (0x10000u | (uint32_t)lane);  // unique when unused
-  const unsigned peers = __match_any_sync(0xffffffffu, tag);
-  if (pred && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-}
-
-// k-th largest key (with low bits cleared after `passes` < 4 passes) among the
-// N keys each thread holds in registers (key 0 = not an element). All threads
-// call. Returns 0 when fewer than k elements exist. Ends with __syncthreads().
+// k-th largest key (low bits cleared when passes < 4) among the N keys each
+// thread holds (key 0 = not an element). Histograms are private per warp
+// (`whist`, 256 words per warp) and summed per pass, so equal keys only
+// contend within a warp. Returns 0 when fewer than k elements exist. All
+// threads call; ends with __syncthreads().
 template <int N>
-__device__ uint32_t cta_kth_largest_regs(const uint32_t (&keys)[N], int k, int passes,
-                                         uint32_t* hist, int* sh) {
+__device__ uint32_t cta_kth_largest_warphist(const uint32_t (&keys)[N], int k, int passes,
+                                             uint32_t* whist, uint32_t* hist, int* sh) {
   uint32_t prefix = 0u, mask = 0u;
   int krem = k;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
 #pragma unroll 1
   for (int pass = 0; pass < passes; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+    for (int i = threadIdx.x; i < nw * 256; i += blockDim.x) whist[i] = 0u;
     __syncthreads();
+    uint32_t* mine = whist + warp * 256;
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const bool in = keys[j] != 0u && (keys[j] & mask) == prefix;
-      hist_add_aggregated(hist, in, (keys[j] >> shift) & 255u);
+    for (int j = 0; j < N; ++j)
+      if (keys[j] != 0u && (keys[j] & mask) == prefix) atomicAdd(&mine[(keys[j] >> shift) & 255u], 1u);
+    __syncthreads();
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+      uint32_t s = 0u;
+      for (int w = 0; w < nw; ++w) s += whist[w * 256 + b];
+      hist[b] = s;
     }
     __syncthreads();
     if (warp == 0) {
@@ -114,15 +117,75 @@ __device__ uint32_t cta_kth_largest_regs(const uint32_t (&keys)[N], int k, int p
   return prefix;
 }
 
+// Warp state carried through the stream loop (warp-uniform).
+struct TlWarp {
+  int count;
+  float theta;
+  int overflow;
+  int nonfinite;  // an exact value of this lane was NaN or +inf
+};
+
+// Rare path of the stream loop, out of line: the lanes' candidates among one
+// step's 16 values (4 float4, columns col0 + 4*u*TL_THREADS ... ) are made
+// exact (penalties) and appended to the warp buffer. `x` holds raw logits.
+// With `all_exact` (a penalty that can raise a value) every value is made
+// exact; otherwise only those at or above the threshold, or not finite.
+__device__ __noinline__ TlWarp tl_candidates(TlWarp st, const Penalty* P, float scale, float4 x0,
+                                             float4 x1, float4 x2, float4 x3, int col0,
+                                             int nvalid, float* wv, int* wi, int K,
+                                             bool all_exact) {
+  const float4 xs[4] = {x0, x1, x2, x3};
+  float ev[16];
+  uint32_t mine = 0u;  // bit (u*4+j): candidate
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float r[4] = {xs[u].x, xs[u].y, xs[u].z, xs[u].w};
+    const int col = col0 + 4 * u * TL_THREADS;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v = -INFINITY;
+      if (u < nvalid) {
+        v = __fmul_rn(r[j], scale);
+        // exact value near the threshold, and wherever raw*scale is not finite
+        if ((all_exact || v >= st.theta || !(v < INFINITY)) && (P->rep || P->cnt))
+          v = __fmul_rn(adjust(*P, r[j], col + j), scale);
+        if (!(v < INFINITY)) {
+          st.nonfinite = 1;
+          v = -INFINITY;
+        }
+      }
+      ev[u * 4 + j] = v;
+      if (v >= st.theta) mine |= 1u << (u * 4 + j);
+    }
+  }
+  uint32_t any = __reduce_or_sync(0xffffffffu, mine);
+  while (any != 0u) {
+    const int bit = __ffs(any) - 1;
+    any &= any - 1u;
+    float v = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (t == bit) v = ev[t];
+    const int col = col0 + 4 * (bit >> 2) * TL_THREADS + (bit & 3);
+    bool ovf = st.overflow != 0;
+    warp_append_reg(((mine >> bit) & 1u) && v >= st.theta, canon(v), col, wv, wi, K, st.count,
+                    st.theta, ovf);
+    st.overflow = ovf ? 1 : 0;
+  }
+  return st;
+}
+
 template <bool kCounts>
-__global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(TL_THREADS, 2)
+    topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* wvall = reinterpret_cast<float*>(smem);                           // [W][WCAP]
   int* wiall = reinterpret_cast<int*>(wvall + TL_WARPS * TW_WCAP);         // [W][WCAP]
   float* cv = reinterpret_cast<float*>(wiall + TL_WARPS * TW_WCAP);        // [CAPB]
   int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                         // [CAPB]
-  unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);   // 32 KiB
-  uint32_t* hist = reinterpret_cast<uint32_t*>(work + 32768);              // [256]
+  unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);   // TL_WORK
+  uint32_t* whist = reinterpret_cast<uint32_t*>(work);                     // [W][256] in work
+  uint32_t* hist = reinterpret_cast<uint32_t*>(work + TL_WORK);            // [256]
   uint32_t* bitmap = hist + 256;
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
 
@@ -131,6 +194,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_co
   __shared__ int s_sh[2];
   __shared__ float s_theta0;
   __shared__ uint32_t s_state;
+  __shared__ Penalty s_pen;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
@@ -143,14 +207,14 @@ __global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_co
 
   Penalty P;
   const bool hist_ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
-  const bool pen_active = P.rep || P.cnt;
-  const bool pen_lowers = !(P.rep && P.pen < 1.0f) && !(P.cnt && (P.freq < 0.0f || P.pres < 0.0f));
-  auto val = [&](float l, int col) -> float { return __fmul_rn(adjust(P, l, col), scale); };
-
   if (tid == 0) {
+    s_pen = P;
     s_nonfinite = 0;
     s_overflow = 0;
   }
+  const bool pen_active = P.rep || P.cnt;
+  const bool pen_lowers = !(P.rep && P.pen < 1.0f) && !(P.cnt && (P.freq < 0.0f || P.pres < 0.0f));
+  auto val = [&](float l, int col) -> float { return __fmul_rn(adjust(P, l, col), scale); };
   if (a.probs) {
     float* prow = a.probs + (size_t)row * V;
     for (int c = c0 + tid; c < c1; c += TL_THREADS) prow[c] = 0.0f;
@@ -166,43 +230,46 @@ __global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_co
 
   float* wv = wvall + warp * TW_WCAP;
   int* wi = wiall + warp * TW_WCAP;
-  int count = 0;
-  bool tie_ovf = false;
+  TlWarp st{0, -INFINITY, 0, 0};
   bool nonfinite = false;
 
-  // ---- first batch: load, exact values, sample select ----------------------
+  // ---- first step: exact values, per-thread maxima -> theta0 ----------------
   float4 x[TL_UNROLL];
-  uint32_t skeys[TL_UNROLL * 4];
 #pragma unroll
   for (int u = 0; u < TL_UNROLL; ++u) {
     const int q = tid + u * TL_THREADS;
     x[u] = (hist_ok && q < n4) ? __ldcs(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-#pragma unroll
-  for (int u = 0; u < TL_UNROLL; ++u) {
-    const int q = tid + u * TL_THREADS;
-    const bool valid = hist_ok && q < n4;
-    const int col = a0 + 4 * q;
-    float e[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float v = valid ? val(e[j], col + j) : -INFINITY;
-      if (!(v < INFINITY)) {
-        nonfinite = nonfinite || valid;
-        v = -INFINITY;
-      }
-      e[j] = v;
-      skeys[u * 4 + j] = valid ? fkey(canon(v)) : 0u;
-    }
-    x[u] = make_float4(e[0], e[1], e[2], e[3]);  // x now holds exact values
-  }
   {
-    const uint32_t key = cta_kth_largest_regs(skeys, K, 2, hist, s_sh);
+    float tmax = -INFINITY;
+    bool have = false;
+#pragma unroll
+    for (int u = 0; u < TL_UNROLL; ++u) {
+      const int q = tid + u * TL_THREADS;
+      if (hist_ok && q < n4) {
+        const int col = a0 + 4 * q;
+        const float e[4] = {val(x[u].x, col), val(x[u].y, col + 1), val(x[u].z, col + 2),
+                            val(x[u].w, col + 3)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (e[j] < INFINITY) {
+            tmax = have ? fmaxf(tmax, e[j]) : e[j];
+            have = true;
+          } else if (e[j] == e[j] || e[j] == INFINITY) {
+            nonfinite = true;  // +inf
+          } else {
+            nonfinite = true;  // NaN
+          }
+        }
+      }
+    }
+    uint32_t k1[1] = {have ? fkey(canon(tmax)) : 0u};
+    const uint32_t key = cta_kth_largest_warphist(k1, K, 4, whist, hist, s_sh);
     // keys at or below the key of -inf decode to NaN patterns: accept all
     if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
   }
   __syncthreads();
-  float theta_w = s_theta0;
+  st.theta = s_theta0;
 
   // head/tail scalars (<= 6) go to warp 0's buffer
   if (warp == 0 && hist_ok) {
@@ -218,76 +285,52 @@ __global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_co
         v = -INFINITY;
       }
     }
-    warp_append_reg(act && v >= theta_w, canon(v), col, wv, wi, K, count, theta_w, tie_ovf);
-  }
-  // candidates of the first batch (exact values already)
-#pragma unroll
-  for (int u = 0; u < TL_UNROLL; ++u) {
-    const int q = tid + u * TL_THREADS;
-    const bool valid = hist_ok && q < n4;
-    const int col = a0 + 4 * q;
-    const bool any = valid && (x[u].x >= theta_w || x[u].y >= theta_w || x[u].z >= theta_w ||
-                               x[u].w >= theta_w);
-    if (__any_sync(0xffffffffu, any)) {
-      const float e[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        warp_append_reg(valid && e[j] >= theta_w, canon(e[j]), col + j, wv, wi, K, count, theta_w,
-                        tie_ovf);
-    }
+    bool ovf = false;
+    warp_append_reg(act && v >= st.theta, canon(v), col, wv, wi, K, st.count, st.theta, ovf);
+    st.overflow = ovf ? 1 : 0;
   }
 
-  // ---- stream the rest ---------------------------------------------------------
+  // ---- stream: the first step's values are still in registers ---------------
   if (hist_ok) {
 #pragma unroll 1
-    for (int base = tid + TL_STEP; base - tid < n4; base += TL_STEP) {
+    for (int base = tid; base - tid < n4; base += TL_STEP) {
+      if (base != tid) {
 #pragma unroll
-      for (int u = 0; u < TL_UNROLL; ++u) {
-        const int q = base + u * TL_THREADS;
-        x[u] = q < n4 ? __ldcs(body + q) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        for (int u = 0; u < TL_UNROLL; ++u) {
+          const int q = base + u * TL_THREADS;
+          x[u] = q < n4 ? __ldcs(body + q)
+                        : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
       }
+      const int nvalid = min(TL_UNROLL, max(0, (n4 - base + TL_THREADS - 1) / TL_THREADS));
+      bool cand = false;
+      bool bad = false;
 #pragma unroll
       for (int u = 0; u < TL_UNROLL; ++u) {
-        const int q = base + u * TL_THREADS;
-        const bool valid = q < n4;
-        const int col = a0 + 4 * q;
-        float vv[4] = {__fmul_rn(x[u].x, scale), __fmul_rn(x[u].y, scale),
-                       __fmul_rn(x[u].z, scale), __fmul_rn(x[u].w, scale)};
-        if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
-            !(vv[3] < INFINITY))
-          nonfinite = true;
-        bool exact = !pen_active;
-        if (pen_active && !pen_lowers && valid && penalty_bits4(P, col) != 0u) {
-          // a penalty that can raise a value: exact values up front
-          vv[0] = val(x[u].x, col);
-          vv[1] = val(x[u].y, col + 1);
-          vv[2] = val(x[u].z, col + 2);
-          vv[3] = val(x[u].w, col + 3);
-          if (!(vv[0] < INFINITY) || !(vv[1] < INFINITY) || !(vv[2] < INFINITY) ||
-              !(vv[3] < INFINITY))
-            nonfinite = true;
-          exact = true;
-        }
-        const bool any = valid && (vv[0] >= theta_w || vv[1] >= theta_w || vv[2] >= theta_w ||
-                                   vv[3] >= theta_w);
-        if (__any_sync(0xffffffffu, any)) {
-          if (any && !exact) {  // exact penalised values near the threshold only
-            vv[0] = val(x[u].x, col);
-            vv[1] = val(x[u].y, col + 1);
-            vv[2] = val(x[u].z, col + 2);
-            vv[3] = val(x[u].w, col + 3);
-          }
+        const float v0 = __fmul_rn(x[u].x, scale), v1 = __fmul_rn(x[u].y, scale);
+        const float v2 = __fmul_rn(x[u].z, scale), v3 = __fmul_rn(x[u].w, scale);
+        // NaN or +inf: !(v < inf)
+        bad = bad || !(v0 < INFINITY) || !(v1 < INFINITY) || !(v2 < INFINITY) || !(v3 < INFINITY);
+        cand = cand || v0 >= st.theta || v1 >= st.theta || v2 >= st.theta || v3 >= st.theta;
+      }
+      // NaN/+inf take the exact path, which decides (a penalty can bring an
+      // overflowed raw*scale back to a finite value)
+      bool force = bad;
+      if (pen_active && !pen_lowers) {
+        // a penalty that can raise a value: penalised ids always take the exact path
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            warp_append_reg(valid && vv[j] >= theta_w && vv[j] < INFINITY, canon(vv[j]), col + j,
-                            wv, wi, K, count, theta_w, tie_ovf);
-        }
+        for (int u = 0; u < TL_UNROLL; ++u)
+          if (u < nvalid && penalty_bits4(P, a0 + 4 * (base + u * TL_THREADS)) != 0u) force = true;
+      }
+      if (__any_sync(0xffffffffu, (cand || force) && nvalid > 0)) {
+        st = tl_candidates(st, &s_pen, scale, x[0], x[1], x[2], x[3], a0 + 4 * base, nvalid, wv,
+                           wi, K, pen_active && !pen_lowers);
       }
     }
   }
-  if (nonfinite) s_nonfinite = 1;
-  if (tie_ovf && lane == 0) s_overflow = 1;
-  if (lane == 0) s_wn[warp] = count;
+  if (nonfinite || st.nonfinite) s_nonfinite = 1;
+  if (st.overflow && lane == 0) s_overflow = 1;
+  if (lane == 0) s_wn[warp] = st.count;
   __syncwarp();
   __syncthreads();
 
@@ -301,12 +344,11 @@ __global__ void __launch_bounds__(TL_THREADS, 2) topk_ldg_kernel(const __grid_co
     uint32_t wk[TW_WCAP / 32];
 #pragma unroll
     for (int r = 0; r < TW_WCAP / 32; ++r) {
-      // thread tid covers entries tid + r*512 of the flattened [W][WCAP] buffers
-      const int i = tid + r * TL_THREADS;
+      const int i = tid + r * TL_THREADS;  // flattened [W][WCAP]
       const int w = i / TW_WCAP, e = i % TW_WCAP;
       wk[r] = e < s_wn[w] ? fkey(wvall[i]) : 0u;
     }
-    const uint32_t key = cta_kth_largest_regs(wk, K, 4, hist, s_sh);
+    const uint32_t key = cta_kth_largest_warphist(wk, K, 4, whist, hist, s_sh);
     if (tid == 0) {
       s_count = 0;
       s_ovf = 0;
