@@ -32,7 +32,8 @@ constexpr int TL_WARPS = TL_THREADS / 32;
 constexpr int TL_UNROLL = 4;                       // float4 loads in flight per thread
 constexpr int TL_STEP = TL_THREADS * TL_UNROLL;    // float4 per CTA step
 constexpr int TL_KMAX = 64;
-constexpr int TL_WORK = 32768;                     // finish / merge / histogram work area
+constexpr int TL_WORK = 32768;                     // finish / merge / histogram / queue area
+constexpr int TL_QCAP = 256;                       // queued float4 indices per warp
 
 inline size_t tl_smem_bytes(int bm_words, int h_cap) {
   return (size_t)TL_WARPS * TW_WCAP * 8      // warp buffers
@@ -117,64 +118,6 @@ __device__ uint32_t cta_kth_largest_warphist(const uint32_t (&keys)[N], int k, i
   return prefix;
 }
 
-// Warp state carried through the stream loop (warp-uniform).
-struct TlWarp {
-  int count;
-  float theta;
-  int overflow;
-  int nonfinite;  // an exact value of this lane was NaN or +inf
-};
-
-// Rare path of the stream loop, out of line: the lanes' candidates among one
-// step's 16 values (4 float4, columns col0 + 4*u*TL_THREADS ... ) are made
-// exact (penalties) and appended to the warp buffer. `x` holds raw logits.
-// With `all_exact` (a penalty that can raise a value) every value is made
-// exact; otherwise only those at or above the threshold, or not finite.
-__device__ __noinline__ TlWarp tl_candidates(TlWarp st, const Penalty* P, float scale, float4 x0,
-                                             float4 x1, float4 x2, float4 x3, int col0,
-                                             int nvalid, float* wv, int* wi, int K,
-                                             bool all_exact) {
-  const float4 xs[4] = {x0, x1, x2, x3};
-  float ev[16];
-  uint32_t mine = 0u;  // bit (u*4+j): candidate
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const float r[4] = {xs[u].x, xs[u].y, xs[u].z, xs[u].w};
-    const int col = col0 + 4 * u * TL_THREADS;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float v = -INFINITY;
-      if (u < nvalid) {
-        v = __fmul_rn(r[j], scale);
-        // exact value near the threshold, and wherever raw*scale is not finite
-        if ((all_exact || v >= st.theta || !(v < INFINITY)) && (P->rep || P->cnt))
-          v = __fmul_rn(adjust(*P, r[j], col + j), scale);
-        if (!(v < INFINITY)) {
-          st.nonfinite = 1;
-          v = -INFINITY;
-        }
-      }
-      ev[u * 4 + j] = v;
-      if (v >= st.theta) mine |= 1u << (u * 4 + j);
-    }
-  }
-  uint32_t any = __reduce_or_sync(0xffffffffu, mine);
-  while (any != 0u) {
-    const int bit = __ffs(any) - 1;
-    any &= any - 1u;
-    float v = -INFINITY;
-#pragma unroll
-    for (int t = 0; t < 16; ++t)
-      if (t == bit) v = ev[t];
-    const int col = col0 + 4 * (bit >> 2) * TL_THREADS + (bit & 3);
-    bool ovf = st.overflow != 0;
-    warp_append_reg(((mine >> bit) & 1u) && v >= st.theta, canon(v), col, wv, wi, K, st.count,
-                    st.theta, ovf);
-    st.overflow = ovf ? 1 : 0;
-  }
-  return st;
-}
-
 template <bool kCounts>
 __global__ void __launch_bounds__(TL_THREADS, 2)
     topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
@@ -230,16 +173,12 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
 
   float* wv = wvall + warp * TW_WCAP;
   int* wi = wiall + warp * TW_WCAP;
-  TlWarp st{0, -INFINITY, 0, 0};
+  int count = 0;
+  float theta = -INFINITY;
+  bool tie_ovf = false;
   bool nonfinite = false;
 
-  // ---- first step: exact values, per-thread maxima -> theta0 ----------------
-  float4 x[TL_UNROLL];
-#pragma unroll
-  for (int u = 0; u < TL_UNROLL; ++u) {
-    const int q = tid + u * TL_THREADS;
-    x[u] = (hist_ok && q < n4) ? __ldcs(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  // ---- sample: exact values of the first step, per-thread maxima -> theta0 --
   {
     float tmax = -INFINITY;
     bool have = false;
@@ -247,18 +186,15 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     for (int u = 0; u < TL_UNROLL; ++u) {
       const int q = tid + u * TL_THREADS;
       if (hist_ok && q < n4) {
+        const float4 x = __ldcs(body + q);
         const int col = a0 + 4 * q;
-        const float e[4] = {val(x[u].x, col), val(x[u].y, col + 1), val(x[u].z, col + 2),
-                            val(x[u].w, col + 3)};
+        const float e[4] = {val(x.x, col), val(x.y, col + 1), val(x.z, col + 2),
+                            val(x.w, col + 3)};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (e[j] < INFINITY) {
             tmax = have ? fmaxf(tmax, e[j]) : e[j];
             have = true;
-          } else if (e[j] == e[j] || e[j] == INFINITY) {
-            nonfinite = true;  // +inf
-          } else {
-            nonfinite = true;  // NaN
           }
         }
       }
@@ -269,7 +205,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
   }
   __syncthreads();
-  st.theta = s_theta0;
+  theta = s_theta0;
 
   // head/tail scalars (<= 6) go to warp 0's buffer
   if (warp == 0 && hist_ok) {
@@ -285,52 +221,79 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
         v = -INFINITY;
       }
     }
-    bool ovf = false;
-    warp_append_reg(act && v >= st.theta, canon(v), col, wv, wi, K, st.count, st.theta, ovf);
-    st.overflow = ovf ? 1 : 0;
+    warp_append_reg(act && v >= theta, canon(v), col, wv, wi, K, count, theta, tie_ovf);
   }
 
-  // ---- stream: the first step's values are still in registers ---------------
-  if (hist_ok) {
+  // ---- stream -----------------------------------------------------------------
+  // The loop only queues the index of every float4 that may hold a candidate
+  // (raw*scale >= theta, a superset when penalties only lower values), a NaN or
+  // +inf, or -- for penalties that can raise a value -- a penalised id. The
+  // queue is drained outside the loop: exact values, then warp appends.
+  int* queue = reinterpret_cast<int*>(work) + warp * TL_QCAP;
+  const bool force_pen = pen_active && !pen_lowers;
+  int qn = 0;
+  int base = tid;
+  bool more = hist_ok;
+  while (more) {
+    more = false;
 #pragma unroll 1
-    for (int base = tid; base - tid < n4; base += TL_STEP) {
-      if (base != tid) {
-#pragma unroll
-        for (int u = 0; u < TL_UNROLL; ++u) {
-          const int q = base + u * TL_THREADS;
-          x[u] = q < n4 ? __ldcs(body + q)
-                        : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        }
-      }
-      const int nvalid = min(TL_UNROLL, max(0, (n4 - base + TL_THREADS - 1) / TL_THREADS));
-      bool cand = false;
-      bool bad = false;
+    for (; base - tid < n4; base += TL_STEP) {
+      float4 x[TL_UNROLL];
 #pragma unroll
       for (int u = 0; u < TL_UNROLL; ++u) {
+        const int q = base + u * TL_THREADS;
+        x[u] = q < n4 ? __ldcs(body + q) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+#pragma unroll
+      for (int u = 0; u < TL_UNROLL; ++u) {
+        const int q = base + u * TL_THREADS;
         const float v0 = __fmul_rn(x[u].x, scale), v1 = __fmul_rn(x[u].y, scale);
         const float v2 = __fmul_rn(x[u].z, scale), v3 = __fmul_rn(x[u].w, scale);
-        // NaN or +inf: !(v < inf)
-        bad = bad || !(v0 < INFINITY) || !(v1 < INFINITY) || !(v2 < INFINITY) || !(v3 < INFINITY);
-        cand = cand || v0 >= st.theta || v1 >= st.theta || v2 >= st.theta || v3 >= st.theta;
+        bool flag = v0 >= theta || v1 >= theta || v2 >= theta || v3 >= theta ||
+                    !(v0 < INFINITY) || !(v1 < INFINITY) || !(v2 < INFINITY) || !(v3 < INFINITY);
+        if (force_pen && q < n4 && penalty_bits4(P, a0 + 4 * q) != 0u) flag = true;
+        flag = flag && q < n4;
+        const unsigned b = __ballot_sync(0xffffffffu, flag);
+        if (b != 0u) {
+          if (flag) queue[qn + __popc(b & ((1u << lane) - 1u))] = q;
+          qn += __popc(b);
+        }
       }
-      // NaN/+inf take the exact path, which decides (a penalty can bring an
-      // overflowed raw*scale back to a finite value)
-      bool force = bad;
-      if (pen_active && !pen_lowers) {
-        // a penalty that can raise a value: penalised ids always take the exact path
-#pragma unroll
-        for (int u = 0; u < TL_UNROLL; ++u)
-          if (u < nvalid && penalty_bits4(P, a0 + 4 * (base + u * TL_THREADS)) != 0u) force = true;
-      }
-      if (__any_sync(0xffffffffu, (cand || force) && nvalid > 0)) {
-        st = tl_candidates(st, &s_pen, scale, x[0], x[1], x[2], x[3], a0 + 4 * base, nvalid, wv,
-                           wi, K, pen_active && !pen_lowers);
+      if (qn > TL_QCAP - 32 * TL_UNROLL) {
+        base += TL_STEP;
+        more = true;
+        break;
       }
     }
+    // drain: exact values of the queued float4s, appended to the warp buffer
+    __syncwarp();
+    for (int i0 = 0; i0 < qn; i0 += 32) {
+      const int i = i0 + lane;
+      const bool valid = i < qn;
+      const int q = valid ? queue[i] : 0;
+      const float4 x = valid ? __ldcg(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int col = a0 + 4 * q;
+      float e[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = valid ? val(e[j], col + j) : -INFINITY;
+        if (!(v < INFINITY)) {
+          nonfinite = nonfinite || valid;
+          v = -INFINITY;
+        }
+        e[j] = v;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        warp_append_reg(valid && e[j] >= theta, canon(e[j]), col + j, wv, wi, K, count, theta,
+                        tie_ovf);
+    }
+    __syncwarp();
+    qn = 0;
   }
-  if (nonfinite || st.nonfinite) s_nonfinite = 1;
-  if (st.overflow && lane == 0) s_overflow = 1;
-  if (lane == 0) s_wn[warp] = st.count;
+  if (nonfinite) s_nonfinite = 1;
+  if (tie_ovf && lane == 0) s_overflow = 1;
+  if (lane == 0) s_wn[warp] = count;
   __syncwarp();
   __syncthreads();
 
