@@ -200,7 +200,9 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       }
     }
     uint32_t k1[1] = {have ? fkey(canon(tmax)) : 0u};
-    const uint32_t key = cta_kth_largest_warphist(k1, K, 4, whist, hist, s_sh);
+    // two radix passes: the K-th largest maximum with its low 16 key bits
+    // cleared, still a lower bound of the segment's K-th largest value
+    const uint32_t key = cta_kth_largest_warphist(k1, K, 2, whist, hist, s_sh);
     // keys at or below the key of -inf decode to NaN patterns: accept all
     if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
   }
