@@ -41,6 +41,10 @@ __device__ __forceinline__ uint32_t fkey(float v) {
   uint32_t b = __float_as_uint(v);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
+// fkey packed into a float's bits / back, so atomicMin on the bits orders by value
+__device__ __forceinline__ float fkey_as_float(float v) { return __uint_as_float(fkey(v)); }
+__device__ __forceinline__ float kval(uint32_t k);
+__device__ __forceinline__ float kval_from_float(float k) { return kval(__float_as_uint(k)); }
 __device__ __forceinline__ float kval(uint32_t k) {
   uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
   return __uint_as_float(b);

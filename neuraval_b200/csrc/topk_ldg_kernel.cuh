@@ -118,6 +118,157 @@ __device__ uint32_t cta_kth_largest_warphist(const uint32_t (&keys)[N], int k, i
   return prefix;
 }
 
+
+constexpr int TL_NB = 1024;   // linear bins of the selection histograms (2 per thread)
+
+// k-th largest of the values held N per thread (valid[j] marks real values;
+// -inf, NaN and +inf must not be marked), via one histogram of TL_NB linear
+// bins over [lo, hi] (bin 0 holds the largest values).
+//  exact == false: returns a lower bound of the k-th largest (the smallest
+//                  value in its bin); *cnt_total = number of marked values.
+//  exact == true : returns the k-th largest exactly; values of its bin are
+//                  ranked in shared memory (`tmp`, >= TL_WORK bytes minus the
+//                  histogram) and, when that bin is crowded, by a radix select.
+// Returns -inf when fewer than k values are marked. All threads call.
+template <int N>
+__device__ float cta_select_linear(const float (&v)[N], const bool (&valid)[N], int k, bool exact,
+                                   unsigned char* work, uint32_t* hist256, int* sh) {
+  __shared__ float s_red[2][TL_WARPS];
+  __shared__ int s_cnt[TL_WARPS];
+  __shared__ float s_hi, s_lo, s_res;
+  __shared__ int s_bstar, s_above, s_nbin, s_total;
+  __shared__ uint32_t s_minkey;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t* bins = reinterpret_cast<uint32_t*>(work);              // [TL_NB]
+  float* binv = reinterpret_cast<float*>(work + TL_NB * 4);        // values of bin b*
+  const int binv_cap = (TL_WORK - TL_NB * 4) / 4;
+  // 1. max, min, count
+  float hi = -INFINITY, lo = INFINITY;
+  int c = 0;
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (valid[j]) {
+      hi = fmaxf(hi, v[j]);
+      lo = fminf(lo, v[j]);
+      ++c;
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+  if (lane == 0) {
+    s_red[0][warp] = hi;
+    s_red[1][warp] = lo;
+    s_cnt[warp] = c;
+  }
+  for (int i = tid; i < TL_NB; i += blockDim.x) bins[i] = 0u;
+  __syncthreads();
+  if (tid == 0) {
+    float h = -INFINITY, l = INFINITY;
+    int t = 0;
+    for (int w = 0; w < TL_WARPS; ++w) {
+      h = fmaxf(h, s_red[0][w]);
+      l = fminf(l, s_red[1][w]);
+      t += s_cnt[w];
+    }
+    s_hi = h;
+    s_lo = l;
+    s_total = t;
+    s_nbin = 0;
+  }
+  __syncthreads();
+  hi = s_hi;
+  lo = s_lo;
+  const int total = s_total;
+  if (total < k) return -INFINITY;
+  if (!(hi > lo)) return hi;  // all marked values equal
+  const float sc = __fdiv_rn((float)TL_NB, __fsub_rn(hi, lo));
+  auto bin_of = [&](float x) {
+    const float f = __fmul_rn(__fsub_rn(hi, x), sc);  // monotone: larger x -> smaller bin
+    const int b = (int)f;
+    return b < TL_NB - 1 ? b : TL_NB - 1;
+  };
+  // 2. histogram
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (valid[j]) atomicAdd(&bins[bin_of(v[j])], 1u);
+  __syncthreads();
+  // 3. first bin where the count from the top reaches k: CTA-wide scan over
+  //    the bins, TL_NB / blockDim per thread
+  {
+    constexpr int PER = TL_NB / TL_THREADS;
+    int cb[PER];
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      cb[j] = (int)bins[tid * PER + j];
+      sum += cb[j];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) s_cnt[warp] = incl;
+    __syncthreads();
+    int wbase = 0;
+    for (int w = 0; w < warp; ++w) wbase += s_cnt[w];
+    const int excl = wbase + incl - sum;
+    if (excl < k && k <= excl + sum) {
+      int run = excl;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        if (run + cb[j] >= k) {
+          s_bstar = tid * PER + j;
+          s_above = run;
+          break;
+        }
+        run += cb[j];
+      }
+    }
+  }
+  if (tid == 0) {
+    s_res = INFINITY;
+    s_minkey = 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  const int bstar = s_bstar;
+  const int above = s_above;
+  // 4. the values of bin b*
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (valid[j] && bin_of(v[j]) == bstar) {
+      const int slot = atomicAdd(&s_nbin, 1);
+      if (slot < binv_cap) binv[slot] = v[j];
+      if (!exact) atomicMin(&s_minkey, fkey(v[j]));
+    }
+  __syncthreads();
+  if (!exact) return kval(s_minkey);
+  const int nb = s_nbin;
+  const int r = k - above;  // rank of the answer inside bin b* (1-based)
+  if (nb <= 32) {
+    if (warp == 0) {
+      const float x = lane < nb ? binv[lane] : -INFINITY;
+      int gt = 0, ge = 0;
+      for (int i = 0; i < nb; ++i) {
+        const float y = binv[i];
+        gt += y > x;
+        ge += y >= x;
+      }
+      if (lane < nb && gt < r && r <= ge) s_res = x;
+    }
+    __syncthreads();
+    return s_res;
+  }
+  // crowded bin: exact radix select among its values
+  const int n = min(nb, binv_cap);
+  const uint32_t key = cta_kth_largest([&](int i) { return fkey(binv[i]); }, n, r, hist256, sh);
+  return kval(key);
+}
+
 template <bool kCounts>
 __global__ void __launch_bounds__(TL_THREADS, 2)
     topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
@@ -127,7 +278,6 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   float* cv = reinterpret_cast<float*>(wiall + TL_WARPS * TW_WCAP);        // [CAPB]
   int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                         // [CAPB]
   unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);   // TL_WORK
-  uint32_t* whist = reinterpret_cast<uint32_t*>(work);                     // [W][256] in work
   uint32_t* hist = reinterpret_cast<uint32_t*>(work + TL_WORK);            // [256]
   uint32_t* bitmap = hist + 256;
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
@@ -148,6 +298,21 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   const float* lrow = a.logits + (size_t)row * V;
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
 
+  // 16-byte aligned body [a0,a1) as float4; <=3 head and <=3 tail scalars
+  const int head = (int)(((16u - ((uint32_t)(uintptr_t)(lrow + c0) & 15u)) & 15u) >> 2);
+  const int a0 = min(c0 + head, c1);
+  const int a1 = a0 + ((c1 - a0) & ~3);
+  const int n4 = (a1 - a0) >> 2;
+  const float4* body = reinterpret_cast<const float4*>(lrow + a0);
+
+  // the sample's loads go out first; the penalty tables are built meanwhile
+  float4 x0[TL_UNROLL];
+#pragma unroll
+  for (int u = 0; u < TL_UNROLL; ++u) {
+    const int q = tid + u * TL_THREADS;
+    x0[u] = q < n4 ? __ldcs(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
   Penalty P;
   const bool hist_ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
   if (tid == 0) {
@@ -164,13 +329,6 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   }
   __syncthreads();
 
-  // 16-byte aligned body [a0,a1) as float4; <=3 head and <=3 tail scalars
-  const int head = (int)(((16u - ((uint32_t)(uintptr_t)(lrow + c0) & 15u)) & 15u) >> 2);
-  const int a0 = min(c0 + head, c1);
-  const int a1 = a0 + ((c1 - a0) & ~3);
-  const int n4 = (a1 - a0) >> 2;
-  const float4* body = reinterpret_cast<const float4*>(lrow + a0);
-
   float* wv = wvall + warp * TW_WCAP;
   int* wi = wiall + warp * TW_WCAP;
   int count = 0;
@@ -186,25 +344,24 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     for (int u = 0; u < TL_UNROLL; ++u) {
       const int q = tid + u * TL_THREADS;
       if (hist_ok && q < n4) {
-        const float4 x = __ldcs(body + q);
         const int col = a0 + 4 * q;
-        const float e[4] = {val(x.x, col), val(x.y, col + 1), val(x.z, col + 2),
-                            val(x.w, col + 3)};
+        const float e[4] = {val(x0[u].x, col), val(x0[u].y, col + 1), val(x0[u].z, col + 2),
+                            val(x0[u].w, col + 3)};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (e[j] < INFINITY) {
+          if (e[j] < INFINITY && e[j] > -INFINITY) {
             tmax = have ? fmaxf(tmax, e[j]) : e[j];
             have = true;
           }
         }
       }
     }
-    uint32_t k1[1] = {have ? fkey(canon(tmax)) : 0u};
-    // two radix passes: the K-th largest maximum with its low 16 key bits
-    // cleared, still a lower bound of the segment's K-th largest value
-    const uint32_t key = cta_kth_largest_warphist(k1, K, 2, whist, hist, s_sh);
-    // keys at or below the key of -inf decode to NaN patterns: accept all
-    if (tid == 0) s_theta0 = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
+    // the smallest maximum in the bin of the K-th largest maximum: distinct
+    // elements of the segment, so a lower bound of its K-th largest value
+    const float sv[1] = {tmax};
+    const bool sok[1] = {have};
+    const float lb = cta_select_linear(sv, sok, K, false, work, hist, s_sh);
+    if (tid == 0) s_theta0 = lb;
   }
   __syncthreads();
   theta = s_theta0;
@@ -269,11 +426,18 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     }
     // drain: exact values of the queued float4s, appended to the warp buffer
     __syncwarp();
+    int qnext = lane < qn ? queue[lane] : 0;
+    float4 xnext = lane < qn ? __ldcg(body + qnext) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = 0; i0 < qn; i0 += 32) {
       const int i = i0 + lane;
       const bool valid = i < qn;
-      const int q = valid ? queue[i] : 0;
-      const float4 x = valid ? __ldcg(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int q = qnext;
+      const float4 x = xnext;
+      if (i0 + 32 < qn) {  // next batch of loads in flight while this one is processed
+        const bool vn = i + 32 < qn;
+        qnext = vn ? queue[i + 32] : 0;
+        xnext = vn ? __ldcg(body + qnext) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       const int col = a0 + 4 * q;
       float e[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
@@ -306,14 +470,20 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   if (s_overflow) state |= RSTATE_OVERFLOW;
   int m = 0;
   if (state == 0u) {
-    uint32_t wk[TW_WCAP / 32];
+    // exact K-th largest over the warp buffers (finite values; -inf entries
+    // are below any finite K-th value and are all kept when it is -inf)
+    float fv[TW_WCAP / 32];
+    bool fok[TW_WCAP / 32];
+    bool inb[TW_WCAP / 32];
 #pragma unroll
     for (int r = 0; r < TW_WCAP / 32; ++r) {
       const int i = tid + r * TL_THREADS;  // flattened [W][WCAP]
       const int w = i / TW_WCAP, e = i % TW_WCAP;
-      wk[r] = e < s_wn[w] ? fkey(wvall[i]) : 0u;
+      inb[r] = e < s_wn[w];
+      fv[r] = inb[r] ? wvall[i] : -INFINITY;
+      fok[r] = inb[r] && fv[r] > -INFINITY;
     }
-    const uint32_t key = cta_kth_largest_warphist(wk, K, 4, whist, hist, s_sh);
+    const float T = cta_select_linear(fv, fok, K, true, work, hist, s_sh);
     if (tid == 0) {
       s_count = 0;
       s_ovf = 0;
@@ -322,8 +492,8 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
 #pragma unroll
     for (int r = 0; r < TW_WCAP / 32; ++r) {
       const int i = tid + r * TL_THREADS;
-      const bool ok = wk[r] != 0u && wk[r] >= key;
-      warp_append(ok, ok ? wvall[i] : 0.f, ok ? wiall[i] : 0, cv, cid, &s_count, &s_ovf);
+      const bool ok = inb[r] && fv[r] >= T;
+      warp_append(ok, ok ? fv[r] : 0.f, ok ? wiall[i] : 0, cv, cid, &s_count, &s_ovf);
     }
     __syncthreads();
     m = min(s_count, TK_CAPB);
