@@ -567,6 +567,9 @@ __global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(const __
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_list[FV_FIXUP_MAX_LIST];
   __shared__ int s_n;
+  // launched as a programmatic dependent of the top-k kernel: it may start
+  // while that kernel drains, and waits here until its writes are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // one parallel pass collects the marked rows (no dependent loads per row)
   for (int base = 0; base < rows; base += FV_FIXUP_MAX_LIST) {
     if (threadIdx.x == 0) s_n = 0;
@@ -794,8 +797,19 @@ inline int launch_fullvocab(const FvScratch& f, SampleArgs a, int rows, int K, i
   if ((int)smem > max_smem) return 8;
   if (fixup) {
     const int g = rows < fixup_ctas ? rows : fixup_ctas;
-    if (counts) fullvocab_fixup_kernel<true><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
-    else fullvocab_fixup_kernel<false><<<g, FV_THREADS, smem, stream>>>(a, f, K, rows);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(g);
+    cfg.blockDim = dim3(FV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = counts ? cudaLaunchKernelEx(&cfg, fullvocab_fixup_kernel<true>, a, f, K, rows)
+                           : cudaLaunchKernelEx(&cfg, fullvocab_fixup_kernel<false>, a, f, K, rows);
+    return e == cudaSuccess ? 0 : 5;
   } else if (counts) {
     fullvocab_kernel<true><<<rows, FV_THREADS, smem, stream>>>(a, f, K);
   } else {

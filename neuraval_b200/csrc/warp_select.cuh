@@ -188,25 +188,35 @@ __device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const
   }
   const bool any_slow = __any_sync(0xffffffffu, slow);
   __syncwarp();
-  int cutoff = m, sel = 0;
-  float retained = 0.0f;
+  // sequential fp32 sums in sorted order (lane 0; the loads run ahead of
+  // the dependent adds), then the cutoff and draw searches by ballot
   if (lane == 0) {
     float total = 0.0f;
+#pragma unroll 8
     for (int i = 0; i < m; ++i) {
       total = __fadd_rn(total, w[i]);
       S[i] = total;
     }
-    float target = 0.0f;
-    if (a.p.top_p < 1.0f) {
-      target = __fmul_rn(total, a.p.top_p);
-      for (int i = 0; i < m; ++i)
-        if (S[i] >= target) { cutoff = i + 1; break; }
-    }
-    retained = S[cutoff - 1];
-    const float sample = __fmul_rn(a.uniforms[row], retained);
-    sel = cutoff - 1;
-    for (int i = 0; i < cutoff; ++i)
-      if (sample <= S[i]) { sel = i; break; }
+  }
+  __syncwarp();
+  const float total = S[m - 1];
+  int cutoff = m;
+  float target = 0.0f;
+  if (a.p.top_p < 1.0f) {
+    target = __fmul_rn(total, a.p.top_p);
+    const unsigned b0 = __ballot_sync(0xffffffffu, lane < m && S[lane] >= target);
+    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < m && S[lane + 32] >= target);
+    cutoff = b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : m);
+  }
+  const float retained = S[cutoff - 1];
+  const float sample = __fmul_rn(a.uniforms[row], retained);
+  int sel;
+  {
+    const unsigned b0 = __ballot_sync(0xffffffffu, lane < cutoff && sample <= S[lane]);
+    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < cutoff && sample <= S[lane + 32]);
+    sel = b0 ? __ffs(b0) - 1 : (b1 ? 32 + __ffs(b1) - 1 : cutoff - 1);
+  }
+  if (lane == 0) {
     uint32_t f = any_slow ? FLAG_EXP_SLOW : 0u;
     const double tol = 1e-6 * (double)retained;
     if (fabs((double)sample - (double)S[sel]) <= tol ||
@@ -220,9 +230,6 @@ __device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const
     }
     if (a.flags) a.flags[row] = f;
   }
-  cutoff = __shfl_sync(0xffffffffu, cutoff, 0);
-  sel = __shfl_sync(0xffffffffu, sel, 0);
-  retained = __shfl_sync(0xffffffffu, retained, 0);
   // token and the tie flag from the sorted keys
   const int rs = sel >> 5, ls = sel & 31;
   uint64_t ksel = 0, kprev = 0, knext = 0;
