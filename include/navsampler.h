@@ -57,6 +57,8 @@ extern "C" {
 #define NCB_FLAG_NONFINITE 0x8u       /* NaN/+inf value or no finite maximum: token -1 */
 #define NCB_FLAG_EXP_SLOW 0x10u       /* a weight needed the double-double exp path */
 #define NCB_FLAG_BAD_HISTORY 0x20u    /* row history longer than the handle's max: token -1 */
+#define NCB_FLAG_TIES_OVERFLOW 0x40u  /* ncb_sample_rows_noalloc_device only: ties at the k-th value
+                                         exceed its candidate buffers: token -1 */
 
 /* ---- sampling options ----------------------------------------------------
  * Mirrors GenerationOptions (Neuraval/Generation/GenerationOptions.cs:5-19):
@@ -116,6 +118,34 @@ NCB_API int ncb_sample_rows(NcbSampler* sampler, const float* h_logits, int rows
                             const int32_t* h_hist, const int32_t* h_hist_offsets,
                             const float* h_uniforms, const NcbSamplerParams* params,
                             int32_t* h_tokens, uint32_t* h_flags, float* h_probs);
+
+/* Allocation-free variant of ncb_sample_rows_device, with no counterpart in the
+ * reference. For callers that cannot allocate device memory when they sample:
+ * a serving process whose device memory is all owned by its own pool or by
+ * another allocator, or a latency-critical loop that cannot afford the device
+ * synchronisation cudaMalloc implies. It needs no handle and allocates nothing:
+ * its scratch (candidate lists of rows split across CTAs, per-row tickets and
+ * marks) is one file-scope device array of 8 MiB, present on every GPU that
+ * loads the library until the process exits.
+ *   - Runs on the current device. The first call on a device looks up that
+ *     array's device address (cudaGetSymbolAddress) and raises the kernels'
+ *     shared-memory limits; make that first call before any stream capture.
+ *   - Serves greedy rows and top-k <= 64 only; other options return
+ *     NCB_ERROR_CAPACITY, as do rows > 1024 and vocab > 2^24. A row whose
+ *     frequency/presence counting needs more than 4096 history ids comes back
+ *     as token -1 with NCB_FLAG_BAD_HISTORY.
+ *   - Every call reuses the same array (the parts that must start at zero are
+ *     cleared on `stream` at the start of each call): calls that overlap on the
+ *     GPU, from any stream or thread, race and corrupt each other's results.
+ *   - Rows whose ties at the k-th value overflow the candidate buffers, which
+ *     the handle-based entry point resolves with its large full-vocabulary
+ *     scratch, come back as token -1 with NCB_FLAG_TIES_OVERFLOW.
+ * Arguments, outputs and errors are otherwise those of ncb_sample_rows_device. */
+NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int rows, int vocab,
+                                           const int32_t* d_hist, const int32_t* d_hist_offsets,
+                                           const float* d_uniforms,
+                                           const NcbSamplerParams* params, int32_t* d_tokens,
+                                           uint32_t* d_flags, float* d_probs, void* stream);
 
 /* ---- LogitsProcessor, batched, in place on device [rows, vocab] ----------- */
 

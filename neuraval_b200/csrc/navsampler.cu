@@ -535,3 +535,150 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* h, float* d_probs, int ro
 }
 
 }  // extern "C"
+
+// ---- allocation-free sampling -----------------------------------------------
+//
+// Scratch for ncb_sample_rows_noalloc_device lives in one file-scope device
+// array instead of a handle's cudaMalloc'd buffer. Host code cannot use its
+// name as a device address: the address is looked up per device with
+// cudaGetSymbolAddress and passed to the kernels.
+
+namespace {
+
+constexpr int NA_MAX_ROWS = 1024;
+constexpr int NA_MAX_SEGMENTS = 512;   // rows x column segments per call
+constexpr int NA_MAX_HISTORY = 4096;   // per-row ids counted for frequency/presence
+constexpr int NA_MAX_DEVICES = 64;
+
+constexpr size_t na_align(size_t x) { return (x + 255) / 256 * 256; }
+constexpr size_t NA_OFF_CV = 0;
+constexpr size_t NA_OFF_CI = NA_OFF_CV + na_align((size_t)NA_MAX_SEGMENTS * nvs::TK_CAPB * 4);
+constexpr size_t NA_OFF_CN = NA_OFF_CI + na_align((size_t)NA_MAX_SEGMENTS * nvs::TK_CAPB * 4);
+constexpr size_t NA_OFF_GV = NA_OFF_CN + na_align((size_t)NA_MAX_SEGMENTS * 4);
+constexpr size_t NA_OFF_GI = NA_OFF_GV + na_align((size_t)NA_MAX_SEGMENTS * 4);
+// everything from here on must be zero when a call starts
+constexpr size_t NA_OFF_ZERO = NA_OFF_GI + na_align((size_t)NA_MAX_SEGMENTS * 4);
+constexpr size_t NA_OFF_TK = NA_OFF_ZERO;
+constexpr size_t NA_OFF_RS = NA_OFF_TK + na_align((size_t)NA_MAX_ROWS * 4);
+constexpr size_t NA_OFF_FX = NA_OFF_RS + na_align((size_t)NA_MAX_ROWS * 4);
+constexpr size_t NA_OFF_ER = NA_OFF_FX + na_align((size_t)NA_MAX_ROWS * 4);
+constexpr size_t NA_BYTES = NA_OFF_ER + 256;  // 8 MiB + 16 KiB
+
+struct NaDevice {
+  char* base = nullptr;  // device address of g_noalloc_scratch on this device
+  int num_sms = 0;
+  int max_dyn_smem = 0;
+};
+NaDevice g_na_dev[NA_MAX_DEVICES];
+std::mutex g_na_mu;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+namespace nvs {
+// Rows the top-k kernel marked for the full-vocabulary fix-up: without that
+// path's scratch they are reported as -1 / NCB_FLAG_TIES_OVERFLOW.
+__global__ void noalloc_finalize_kernel(int rows, uint32_t* fixup, int32_t* tokens,
+                                        uint32_t* flags) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    if (fixup[r] != 0u) {
+      tokens[r] = -1;
+      if (flags) flags[r] = NCB_FLAG_TIES_OVERFLOW;
+      fixup[r] = 0u;
+    }
+  }
+}
+}  // namespace nvs
+
+extern "C" NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int rows, int vocab,
+                                                      const int32_t* d_hist,
+                                                      const int32_t* d_hist_offsets,
+                                                      const float* d_uniforms,
+                                                      const NcbSamplerParams* prm,
+                                                      int32_t* d_tokens, uint32_t* d_flags,
+                                                      float* d_probs, void* stream_) {
+  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (rows == 0) return set_status(NCB_OK);
+  if (!d_logits || !d_hist_offsets || !d_tokens || (!prm->greedy && !d_uniforms))
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if ((reinterpret_cast<uintptr_t>(d_logits) & 3u) != 0u)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  if (rows > NA_MAX_ROWS || vocab > (1 << 24)) return set_status(NCB_ERROR_CAPACITY);
+  if (!prm->greedy && !(K < vocab && K <= nvs::TL_KMAX)) return set_status(NCB_ERROR_CAPACITY);
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NA_MAX_DEVICES)
+    return set_status(NCB_ERROR_NO_DEVICE);
+  NaDevice nd;
+  {
+    // first call on this device: look up the scratch array's device address
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    if (!g_na_dev[dev].base) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
+        return set_status(NCB_ERROR_INIT_FAILED);
+      int sms = 0, optin = 0;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+              cudaSuccess ||
+          !raise_smem_limits(optin))
+        return set_status(NCB_ERROR_INIT_FAILED);
+      g_na_dev[dev].num_sms = sms;
+      g_na_dev[dev].max_dyn_smem = optin - 4096;
+      g_na_dev[dev].base = static_cast<char*>(ptr);
+    }
+    nd = g_na_dev[dev];
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+
+  nvs::SampleArgs a{};
+  a.logits = d_logits;
+  a.V = vocab;
+  a.hist = d_hist;
+  a.hoff = d_hist_offsets;
+  a.uniforms = d_uniforms;
+  a.p = to_params(prm);
+  a.tokens = d_tokens;
+  a.flags = d_flags;
+  a.probs = d_probs;
+  a.s.cand_v = reinterpret_cast<float*>(nd.base + NA_OFF_CV);
+  a.s.cand_id = reinterpret_cast<int32_t*>(nd.base + NA_OFF_CI);
+  a.s.cand_n = reinterpret_cast<int32_t*>(nd.base + NA_OFF_CN);
+  a.s.gv = reinterpret_cast<float*>(nd.base + NA_OFF_GV);
+  a.s.gi = reinterpret_cast<int32_t*>(nd.base + NA_OFF_GI);
+  a.s.tickets = reinterpret_cast<uint32_t*>(nd.base + NA_OFF_TK);
+  a.s.rowstate = reinterpret_cast<uint32_t*>(nd.base + NA_OFF_RS);
+  a.s.fixup = reinterpret_cast<uint32_t*>(nd.base + NA_OFF_FX);
+  a.s.error_word = reinterpret_cast<uint32_t*>(nd.base + NA_OFF_ER);
+  const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
+  a.h_cap = counts ? NA_MAX_HISTORY : 0;
+
+  // what a previous call may have left behind must start at zero
+  if (cudaMemsetAsync(nd.base + NA_OFF_ZERO, 0, NA_BYTES - NA_OFF_ZERO, stream) != cudaSuccess)
+    return set_status(NCB_ERROR_LAUNCH_FAILED);
+
+  int S = choose_splits(rows, vocab, nd.num_sms, 0);
+  if (rows * S > NA_MAX_SEGMENTS) S = NA_MAX_SEGMENTS / rows > 0 ? NA_MAX_SEGMENTS / rows : 1;
+  a.seg_len = round_up((vocab + S - 1) / S, 4);
+  S = (vocab + a.seg_len - 1) / a.seg_len;
+  a.bm_words = (a.seg_len + 31) / 32 + 1;
+  dim3 grid(S, rows);
+  if (prm->greedy) {
+    const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
+    if ((int)smem > nd.max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
+    if (counts) nvs::greedy_kernel<true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+    else nvs::greedy_kernel<false><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+  } else {
+    const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
+    if ((int)smem > nd.max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
+    if (counts) nvs::topk_ldg_kernel<true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    else nvs::topk_ldg_kernel<false><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return set_status(NCB_ERROR_LAUNCH_FAILED);
+    nvs::noalloc_finalize_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(rows, a.s.fixup,
+                                                                        d_tokens, d_flags);
+  }
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}

@@ -28,6 +28,7 @@ FLAG_TIE_AT_DRAW = 0x4
 FLAG_NONFINITE = 0x8
 FLAG_EXP_SLOW = 0x10
 FLAG_BAD_HISTORY = 0x20
+FLAG_TIES_OVERFLOW = 0x40
 # rows whose token may legitimately differ from the reference's
 PARITY_EXEMPT = FLAG_DRAW_BOUNDARY | FLAG_CUTOFF_BOUNDARY | FLAG_TIE_AT_DRAW
 
@@ -58,6 +59,8 @@ SIGNATURES = {
                                     _P, _P, _P, _P]),
     "ncb_sample_rows": (_I, [_P, _P, _I, _I, _P, _P, _P, ctypes.POINTER(NcbSamplerParams),
                              _P, _P, _P]),
+    "ncb_sample_rows_noalloc_device": (_I, [_P, _I, _I, _P, _P, _P,
+                                            ctypes.POINTER(NcbSamplerParams), _P, _P, _P, _P]),
     "ncb_logits_repetition_penalty_device": (_I, [_P, _P, _I, _I, _P, _P, _F, _P]),
     "ncb_logits_frequency_presence_penalty_device": (_I, [_P, _P, _I, _I, _P, _P, _F, _F, _P]),
     "ncb_logits_temperature_device": (_I, [_P, _P, _I, _I, _F, _P]),
