@@ -18,6 +18,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import sys
 import threading
@@ -81,13 +82,18 @@ def measured_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes per launch of the top-k kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "topk_kernel_zipf_ranked_256x128256.json")
+    """DRAM bytes (read + write) per launch of the top-k kernel, from the committed
+    ncu summary of this workload (its `dram_bytes_per_launch:` line)."""
+    path = os.path.join(ROOT, "profiles", "topk_ldg_kernel_zipf_ranked_256x128256.md")
     try:
         with open(path) as fh:
-            return json.load(fh).get("dram_bytes_per_launch")
-    except Exception:
-        return None
+            for line in fh:
+                m = re.match(r"\s*-?\s*`?dram_bytes_per_launch`?:\s*([0-9]+)", line)
+                if m:
+                    return int(m.group(1))
+    except OSError:
+        pass
+    return None
 
 
 class ClockSampler:
@@ -327,7 +333,7 @@ def main():
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "peak_source": peak_kind,
                             "traffic": profiled_traffic(),
-                            "kernel": "topk_kernel (+ its fix-up launch, timed together)",
+                            "kernel": "topk_ldg_kernel (+ its fix-up launch, timed together)",
                             "algorithmic_bytes_per_launch": bytes_per_launch},
                "e2e": e2e,
                "gpu_launches": 2 * args.steps,
