@@ -57,8 +57,9 @@ extern "C" {
 #define NCB_FLAG_NONFINITE 0x8u       /* NaN/+inf value or no finite maximum: token -1 */
 #define NCB_FLAG_EXP_SLOW 0x10u       /* a weight needed the double-double exp path */
 #define NCB_FLAG_BAD_HISTORY 0x20u    /* row history longer than the handle's max: token -1 */
-#define NCB_FLAG_TIES_OVERFLOW 0x40u  /* ncb_sample_rows_noalloc_device only: ties at the k-th value
-                                         exceed its candidate buffers: token -1 */
+#define NCB_FLAG_TIES_OVERFLOW 0x40u  /* ncb_sample_rows_noalloc_device and vocabulary-shard
+                                         merges only: ties at the k-th value exceed the
+                                         candidate buffers: token -1 */
 
 /* ---- sampling options ----------------------------------------------------
  * Mirrors GenerationOptions (Neuraval/Generation/GenerationOptions.cs:5-19):
@@ -146,6 +147,39 @@ NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int rows, int 
                                            const float* d_uniforms,
                                            const NcbSamplerParams* params, int32_t* d_tokens,
                                            uint32_t* d_flags, float* d_probs, void* stream);
+
+/* ---- vocabulary shards -----------------------------------------------------
+ * No counterpart in the reference (it samples on one CPU thread): a batch whose
+ * vocabulary is split in contiguous column ranges over several GPUs (a
+ * tensor-parallel LM head leaves each GPU its columns of the logits). Each GPU
+ * reduces its columns of every row to one record of
+ * ncb_vocab_shard_record_bytes() bytes; the caller gathers the records of all
+ * shards on every GPU, in column order, as [shards][rows] records (one NCCL
+ * all-gather); each GPU then merges them into the tokens that
+ * ncb_sample_rows_device gives for the whole rows (TokenSampler.cs:10-143).
+ * Served: greedy rows and top-k <= 64 (other options: NCB_ERROR_CAPACITY).
+ * A row whose ties at the global k-th value were cut from a shard's record
+ * (more than 128 - (k-1) equal values) comes back as token -1 with
+ * NCB_FLAG_TIES_OVERFLOW. */
+NCB_API int ncb_vocab_shard_record_bytes(void);
+
+/* d_logits: [rows, ld] fp32 holding columns [col_begin, col_end) of the full
+ * vocabulary `vocab` (ld >= col_end - col_begin); histories hold full-vocabulary
+ * ids. Writes rows records to d_records. col_end - col_begin <= the handle's
+ * max_vocab; rows <= its max_rows. Asynchronous on `stream`. */
+NCB_API int ncb_vocab_shard_candidates_device(NcbSampler* sampler, const float* d_logits,
+                                              int rows, int vocab, int col_begin, int col_end,
+                                              int ld, const int32_t* d_hist,
+                                              const int32_t* d_hist_offsets,
+                                              const NcbSamplerParams* params, void* d_records,
+                                              void* stream);
+
+/* d_records: [shards][rows] records, shard s holding the s-th column range.
+ * shards <= 16. Outputs as ncb_sample_rows_device (no probabilities). */
+NCB_API int ncb_vocab_shard_merge_device(NcbSampler* sampler, const void* d_records, int shards,
+                                         int rows, int vocab, const float* d_uniforms,
+                                         const NcbSamplerParams* params, int32_t* d_tokens,
+                                         uint32_t* d_flags, void* stream);
 
 /* ---- LogitsProcessor, batched, in place on device [rows, vocab] ----------- */
 

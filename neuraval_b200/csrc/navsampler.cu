@@ -19,6 +19,7 @@
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
 #include "topk_ldg_kernel.cuh"
+#include "vocab_merge.cuh"
 
 namespace {
 
@@ -137,6 +138,11 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::topk_ldg_kernel<false>);
   set((const void*)nvs::greedy_kernel<true>);
   set((const void*)nvs::greedy_kernel<false>);
+  set((const void*)nvs::topk_ldg_kernel<true, true>);
+  set((const void*)nvs::topk_ldg_kernel<false, true>);
+  set((const void*)nvs::greedy_kernel<true, true>);
+  set((const void*)nvs::greedy_kernel<false, true>);
+  set((const void*)nvs::vocab_merge_kernel);
   set((const void*)nvs::fullvocab_kernel<true>);
   set((const void*)nvs::fullvocab_kernel<false>);
   set((const void*)nvs::fullvocab_fixup_kernel<true>);
@@ -682,3 +688,108 @@ extern "C" NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int
   }
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
 }
+
+// ---- vocabulary shards ------------------------------------------------------
+//
+// A batch whose vocabulary is split in contiguous column ranges over several
+// GPUs: each GPU reduces its range of every row to a fixed-size record
+// (ncb_vocab_shard_candidates_device), the caller all-gathers the records of
+// all shards in column order, and every GPU merges them
+// (ncb_vocab_shard_merge_device) into the same tokens the single-GPU entry
+// point gives for the whole rows.
+
+extern "C" {
+
+NCB_API int ncb_vocab_shard_record_bytes(void) { return nvs::VS_REC_WORDS * 4; }
+
+NCB_API int ncb_vocab_shard_candidates_device(NcbSampler* h, const float* d_logits, int rows,
+                                              int vocab, int col_begin, int col_end, int ld,
+                                              const int32_t* d_hist,
+                                              const int32_t* d_hist_offsets,
+                                              const NcbSamplerParams* prm, void* d_records,
+                                              void* stream_) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0 || col_begin < 0 ||
+      col_end <= col_begin || col_end > vocab || ld < col_end - col_begin)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (rows == 0) return set_status(NCB_OK);
+  if (!d_logits || !d_hist_offsets || !d_records) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if ((reinterpret_cast<uintptr_t>(d_logits) & 3u) != 0u ||
+      (reinterpret_cast<uintptr_t>(d_records) & 3u) != 0u)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  const int width = col_end - col_begin;
+  if (rows > h->max_rows || width > h->max_vocab) return set_status(NCB_ERROR_CAPACITY);
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  if (!prm->greedy && K > nvs::TL_KMAX) return set_status(NCB_ERROR_CAPACITY);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+
+  nvs::SampleArgs a{};
+  a.logits = d_logits;
+  a.V = vocab;
+  a.hist = d_hist;
+  a.hoff = d_hist_offsets;
+  a.p = to_params(prm);
+  a.s = h->s;
+  a.ld = ld;
+  a.col_lo = col_begin;
+  a.col_hi = col_end;
+  a.shard_out = static_cast<uint32_t*>(d_records);
+  const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
+  a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
+  int S = choose_splits(rows, width, h->num_sms, h->forced_splits);
+  a.seg_len = round_up((width + S - 1) / S, 4);
+  S = (width + a.seg_len - 1) / a.seg_len;
+  if ((size_t)rows * S > (size_t)h->max_ctas) return set_status(NCB_ERROR_CAPACITY);
+  a.bm_words = (a.seg_len + 31) / 32 + 1;
+  dim3 grid(S, rows);
+  if (prm->greedy) {
+    const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
+    if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
+    if (counts) nvs::greedy_kernel<true, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+    else nvs::greedy_kernel<false, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+  } else {
+    const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
+    if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
+    if (counts) nvs::topk_ldg_kernel<true, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    else nvs::topk_ldg_kernel<false, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+  }
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, int shards,
+                                         int rows, int vocab, const float* d_uniforms,
+                                         const NcbSamplerParams* prm, int32_t* d_tokens,
+                                         uint32_t* d_flags, void* stream_) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0 || shards <= 0)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (rows == 0) return set_status(NCB_OK);
+  if (!d_records || !d_tokens || (!prm->greedy && !d_uniforms) ||
+      (reinterpret_cast<uintptr_t>(d_records) & 3u) != 0u)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  if (shards > nvs::VM_MAX_SHARDS || (!prm->greedy && K > nvs::TL_KMAX))
+    return set_status(NCB_ERROR_CAPACITY);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  nvs::MergeArgs m{};
+  m.recs = static_cast<const uint32_t*>(d_records);
+  m.shards = shards;
+  m.rows = rows;
+  m.a.V = vocab;
+  m.a.uniforms = d_uniforms;
+  m.a.p = to_params(prm);
+  m.a.tokens = d_tokens;
+  m.a.flags = d_flags;
+  m.a.s = h->s;
+  const size_t smem = nvs::vm_smem_bytes();
+  if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
+  nvs::vocab_merge_kernel<<<rows, nvs::VM_THREADS, smem, static_cast<cudaStream_t>(stream_)>>>(m);
+  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+}
+
+}  // extern "C"

@@ -17,6 +17,7 @@ constexpr uint32_t FLAG_TIE_AT_DRAW = 0x4u;
 constexpr uint32_t FLAG_NONFINITE = 0x8u;
 constexpr uint32_t FLAG_EXP_SLOW = 0x10u;
 constexpr uint32_t FLAG_BAD_HISTORY = 0x20u;
+constexpr uint32_t FLAG_TIES_OVERFLOW = 0x40u;
 // internal row states carried in scratch between kernels (never returned)
 constexpr uint32_t RSTATE_OVERFLOW = 0x100u;  // candidates (ties) exceed the top-k buffers
 constexpr uint32_t RSTATE_TIMEOUT = 0x200u;   // a bounded wait gave up

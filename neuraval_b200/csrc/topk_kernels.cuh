@@ -18,6 +18,7 @@
 #pragma once
 
 #include "sampler_device.cuh"
+#include "shard_record.cuh"
 
 namespace nvs {
 
@@ -54,6 +55,13 @@ struct SampleArgs {
   int bm_words;         // bitmap words per CTA (columns/32 rounded up, plus one spare)
   int h_cap;            // history ids per CTA in smem (counts only), power of 2
   Scratch s;
+  // vocabulary shards only (kShard kernels): `logits` holds columns
+  // [col_lo, col_hi) of each row with row stride `ld`; `V` stays the full
+  // vocabulary; every row's record goes to shard_out + row * VS_REC_WORDS
+  int ld;
+  int col_lo;
+  int col_hi;
+  uint32_t* shard_out;
 };
 
 // Shared penalty state for the CTA's column range [c0,c1). Returns false when
@@ -130,7 +138,7 @@ __device__ __forceinline__ Best warp_best(Best b) {
   return b;
 }
 
-template <bool kCounts>
+template <bool kCounts, bool kShard = false>
 __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem);
@@ -142,9 +150,10 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
 
   const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const int V = a.V;
-  const int c0 = split * a.seg_len;
-  const int c1 = min(V, c0 + a.seg_len);
-  const float* lrow = a.logits + (size_t)row * V;
+  const int lo = kShard ? a.col_lo : 0, hi = kShard ? a.col_hi : V;
+  const int c0 = lo + split * a.seg_len;
+  const int c1 = min(hi, c0 + a.seg_len);
+  const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * V;
 
   Penalty P;
   const bool ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
@@ -175,6 +184,10 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
   if (S == 1) {
     if (threadIdx.x == 0) {
       Best r = s_w[0];
+      if constexpr (kShard) {
+        write_greedy_record(a.shard_out + (size_t)row * VS_REC_WORDS, r.v, r.i, !ok, s_nan0 != 0);
+        return;
+      }
       int tok = (s_nan0 || r.i < 0) ? 0 : r.i;
       a.tokens[row] = ok ? tok : -1;
       if (a.flags) a.flags[row] = ok ? 0u : FLAG_BAD_HISTORY;
@@ -205,9 +218,13 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
       const uint32_t st = __ldcg(&a.s.rowstate[row]);
       const bool bad = (st & FLAG_BAD_HISTORY) != 0u;
       const bool nan0 = (st & 0x40000000u) != 0u;
-      int tok = (nan0 || r.i < 0) ? 0 : r.i;
-      a.tokens[row] = bad ? -1 : tok;
-      if (a.flags) a.flags[row] = bad ? FLAG_BAD_HISTORY : 0u;
+      if constexpr (kShard) {
+        write_greedy_record(a.shard_out + (size_t)row * VS_REC_WORDS, r.v, r.i, bad, nan0);
+      } else {
+        int tok = (nan0 || r.i < 0) ? 0 : r.i;
+        a.tokens[row] = bad ? -1 : tok;
+        if (a.flags) a.flags[row] = bad ? FLAG_BAD_HISTORY : 0u;
+      }
       a.s.rowstate[row] = 0u;
       a.s.tickets[row] = 0u;
     }

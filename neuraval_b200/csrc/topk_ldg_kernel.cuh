@@ -269,7 +269,7 @@ __device__ float cta_select_linear(const float (&v)[N], const bool (&valid)[N], 
   return kval(key);
 }
 
-template <bool kCounts>
+template <bool kCounts, bool kShard = false>
 __global__ void __launch_bounds__(TL_THREADS, 2)
     topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -293,9 +293,11 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   const int row = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const int V = a.V;
   const int K = min(a.p.top_k, V);
-  const int c0 = split * a.seg_len;
-  const int c1 = min(V, c0 + a.seg_len);
-  const float* lrow = a.logits + (size_t)row * V;
+  const int lo = kShard ? a.col_lo : 0, hi = kShard ? a.col_hi : V;
+  const int c0 = lo + split * a.seg_len;
+  const int c1 = min(hi, c0 + a.seg_len);
+  // shard rows are addressed by global column: lrow[c] for c in [lo, hi)
+  const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * V;
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
 
   // 16-byte aligned body [a0,a1) as float4; <=3 head and <=3 tail scalars
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   const bool pen_active = P.rep || P.cnt;
   const bool pen_lowers = !(P.rep && P.pen < 1.0f) && !(P.cnt && (P.freq < 0.0f || P.pres < 0.0f));
   auto val = [&](float l, int col) -> float { return __fmul_rn(adjust(P, l, col), scale); };
-  if (a.probs) {
+  if (!kShard && a.probs) {
     float* prow = a.probs + (size_t)row * V;
     for (int c = c0 + tid; c < c1; c += TL_THREADS) prow[c] = 0.0f;
   }
@@ -365,6 +367,10 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   }
   __syncthreads();
   theta = s_theta0;
+  // a shard's record holds finite values only: -inf can be a global candidate
+  // only in a row with fewer than K finite values, where it never decides the
+  // token (its weight is exp(-inf) = 0)
+  if constexpr (kShard) theta = fmaxf(theta, -3.40282347e+38f);
 
   // head/tail scalars (<= 6) go to warp 0's buffer
   if (warp == 0 && hist_ok) {
@@ -469,6 +475,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   if (s_nonfinite) state |= FLAG_NONFINITE;
   if (s_overflow) state |= RSTATE_OVERFLOW;
   int m = 0;
+  float kth = -INFINITY;  // the segment's K-th largest value
   if (state == 0u) {
     // exact K-th largest over the warp buffers (finite values; -inf entries
     // are below any finite K-th value and are all kept when it is -inf)
@@ -484,6 +491,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       fok[r] = inb[r] && fv[r] > -INFINITY;
     }
     const float T = cta_select_linear(fv, fok, K, true, work, hist, s_sh);
+    kth = T;
     if (tid == 0) {
       s_count = 0;
       s_ovf = 0;
@@ -501,6 +509,10 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   }
 
   if (S == 1) {
+    if constexpr (kShard) {
+      write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, cv, cid, m, state, kth);
+      return;
+    }
     if (state == 0u && m > 0 && m <= 64) {
       if (warp == 0) finish_row_warp(a, row, cv, cid, m, reinterpret_cast<float*>(work));
     } else {
@@ -540,6 +552,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   const int total = s_tot;
   if (total > TK_CAPB) mstate |= RSTATE_OVERFLOW;
   int mm = 0;
+  float mkth = -INFINITY;
   if (mstate == 0u) {
     int off = 0;
     for (int sp = 0; sp < S; ++sp) {
@@ -553,6 +566,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     }
     __syncthreads();
     const uint32_t key = cta_kth_largest([&](int i) { return fkey(uv[i]); }, total, K, hist, s_sh);
+    mkth = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
     if (tid == 0) {
       s_count = 0;
       s_ovf = 0;
@@ -569,7 +583,9 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   }
   __syncthreads();
   // the union is dead now: the finish reuses the work area
-  if (mstate == 0u && mm > 0 && mm <= 64) {
+  if constexpr (kShard) {
+    write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, cv, cid, mm, mstate, mkth);
+  } else if (mstate == 0u && mm > 0 && mm <= 64) {
     if (warp == 0) finish_row_warp(a, row, cv, cid, mm, reinterpret_cast<float*>(work));
   } else {
     finish_row(a, row, cv, cid, mm, mstate, work);

@@ -1,0 +1,151 @@
+// Merge of vocabulary-shard records (sm_100a): one CTA per row reads the
+// records of all shards ([shards][rows][VS_REC_WORDS], shard order = column
+// order) and finishes the row as the single-GPU kernels do.
+//  - top-k rows: the global K-th largest value over the union of the shards'
+//    candidates (TokenSampler.cs:73-84), every candidate >= it (:88-93), then
+//    the shared finish (sort, exp, sequential sums, top-p, draw; :95-132);
+//  - greedy rows: the first strict maximum over the shards' maxima, id 0 when
+//    global id 0 is NaN (:38-51).
+#pragma once
+
+#include "shard_record.cuh"
+#include "topk_kernels.cuh"
+#include "warp_select.cuh"
+
+namespace nvs {
+
+constexpr int VM_THREADS = 512;
+constexpr int VM_MAX_SHARDS = TK_CAPB / VS_CAP;  // 16: the union fits the candidate list
+constexpr int VM_WORK = 32768;
+
+inline size_t vm_smem_bytes() { return (size_t)TK_CAPB * 8 + VM_WORK + 256 * 4; }
+
+struct MergeArgs {
+  const uint32_t* recs;  // [shards][rows][VS_REC_WORDS]
+  int shards;
+  int rows;
+  SampleArgs a;          // V = full vocabulary, p, uniforms, tokens, flags (probs unused)
+};
+
+__global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_constant__ MergeArgs g) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* cv = reinterpret_cast<float*>(smem);                            // [CAPB]
+  int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                       // [CAPB]
+  unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);  // VM_WORK
+  uint32_t* hist = reinterpret_cast<uint32_t*>(work + VM_WORK);          // [256]
+  __shared__ int s_n[VM_MAX_SHARDS], s_off[VM_MAX_SHARDS + 1];
+  __shared__ uint32_t s_state, s_kth[VM_MAX_SHARDS];
+  __shared__ int s_sh[2], s_count, s_ovf;
+
+  const SampleArgs& a = g.a;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = g.shards;
+  const size_t stride = (size_t)g.rows * VS_REC_WORDS;
+  const uint32_t* rec0 = g.recs + (size_t)row * VS_REC_WORDS;
+
+  if (tid == 0) {
+    uint32_t st = 0u;
+    int off = 0;
+    for (int s = 0; s < G; ++s) {
+      const uint32_t* r = rec0 + s * stride;
+      const int n = min((int)r[0], VS_CAP);
+      s_n[s] = n;
+      s_off[s] = off;
+      s_kth[s] = r[2];
+      off += n;
+      st |= r[1];
+    }
+    s_off[G] = off;
+    s_state = st;
+  }
+  __syncthreads();
+  const uint32_t st = s_state;
+  const int total = s_off[G];
+
+  if (a.p.greedy) {
+    if (warp == 0) {
+      Best b{0.0f, -1};
+      for (int s = lane; s < G; s += 32) {
+        const uint32_t* r = rec0 + s * stride;
+        if (s_n[s] > 0) b = better(b, Best{__uint_as_float(r[VS_HDR]), (int)r[VS_HDR + VS_CAP]});
+      }
+      b = warp_best(b);
+      if (lane == 0) {
+        const bool bad = (st & FLAG_BAD_HISTORY) != 0u;
+        const int tok = ((st & VS_NAN0) || b.i < 0) ? 0 : b.i;
+        a.tokens[row] = bad ? -1 : tok;
+        if (a.flags) a.flags[row] = bad ? FLAG_BAD_HISTORY : 0u;
+      }
+    }
+    return;
+  }
+
+  if (st & (FLAG_NONFINITE | FLAG_BAD_HISTORY)) {
+    finish_row(a, row, cv, cid, 0, st & (FLAG_NONFINITE | FLAG_BAD_HISTORY), work);
+    return;
+  }
+  if (st & VS_OVF_UNKNOWN) {
+    if (tid == 0) {
+      a.tokens[row] = -1;
+      if (a.flags) a.flags[row] = FLAG_TIES_OVERFLOW;
+    }
+    return;
+  }
+  if (total == 0) {  // no finite value in any shard
+    finish_row(a, row, cv, cid, 0, FLAG_NONFINITE, work);
+    return;
+  }
+
+  // union of the shards' candidates
+  float* uv = reinterpret_cast<float*>(work);            // [CAPB]
+  int* uid = reinterpret_cast<int*>(uv + TK_CAPB);        // [CAPB]
+  for (int s = 0; s < G; ++s) {
+    const uint32_t* r = rec0 + s * stride;
+    const int n = s_n[s], o = s_off[s];
+    for (int i = tid; i < n; i += VM_THREADS) {
+      uv[o + i] = __uint_as_float(r[VS_HDR + i]);
+      uid[o + i] = (int)r[VS_HDR + VS_CAP + i];
+    }
+  }
+  __syncthreads();
+  // fewer than K finite values in the whole row: every finite value is a
+  // candidate (key 0 below), the row's -inf values would only add zero weights
+  const int K = min(a.p.top_k, a.V);
+  const uint32_t key = cta_kth_largest([&](int i) { return fkey(uv[i]); }, total, K, hist, s_sh);
+  const float theta = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
+  if (tid == 0) {
+    // a shard that cut ties at its K-th value matters only when that value is
+    // the global K-th value
+    bool cut = false;
+    if (st & VS_OVF_AT_KTH)
+      for (int s = 0; s < G; ++s) {
+        const uint32_t rs = rec0[s * stride + 1];
+        if ((rs & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == theta) cut = true;
+      }
+    s_ovf = cut ? 1 : 0;
+    s_count = 0;
+  }
+  __syncthreads();
+  if (s_ovf) {
+    if (tid == 0) {
+      a.tokens[row] = -1;
+      if (a.flags) a.flags[row] = FLAG_TIES_OVERFLOW;
+    }
+    return;
+  }
+  for (int i0 = 0; i0 < total; i0 += VM_THREADS) {
+    const int i = i0 + tid;
+    const bool ok = i < total && fkey(uv[i]) >= key;
+    warp_append(ok, ok ? uv[i] : 0.f, ok ? uid[i] : 0, cv, cid, &s_count, &s_ovf);
+  }
+  __syncthreads();
+  const int m = min(s_count, TK_CAPB);
+  // the union is dead now: the finish reuses the work area
+  if (m > 0 && m <= 64) {
+    if (warp == 0) finish_row_warp(a, row, cv, cid, m, reinterpret_cast<float*>(work));
+  } else {
+    finish_row(a, row, cv, cid, m, 0u, work);
+  }
+}
+
+}  // namespace nvs

@@ -61,6 +61,11 @@ SIGNATURES = {
                              _P, _P, _P]),
     "ncb_sample_rows_noalloc_device": (_I, [_P, _I, _I, _P, _P, _P,
                                             ctypes.POINTER(NcbSamplerParams), _P, _P, _P, _P]),
+    "ncb_vocab_shard_record_bytes": (_I, []),
+    "ncb_vocab_shard_candidates_device": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P,
+                                               ctypes.POINTER(NcbSamplerParams), _P, _P]),
+    "ncb_vocab_shard_merge_device": (_I, [_P, _P, _I, _I, _I, _P,
+                                          ctypes.POINTER(NcbSamplerParams), _P, _P, _P]),
     "ncb_logits_repetition_penalty_device": (_I, [_P, _P, _I, _I, _P, _P, _F, _P]),
     "ncb_logits_frequency_presence_penalty_device": (_I, [_P, _P, _I, _I, _P, _P, _F, _F, _P]),
     "ncb_logits_temperature_device": (_I, [_P, _P, _I, _I, _F, _P]),

@@ -90,6 +90,31 @@ class CudaTokenSampler:
         check(st, "ncb_sample_rows")
         return tokens, flags, probs
 
+    # ---- vocabulary shards (device tensors) -------------------------------
+    @property
+    def shard_record_bytes(self) -> int:
+        return int(self._lib.ncb_vocab_shard_record_bytes())
+
+    def shard_candidates_device(self, logits_shard, vocab: int, col_begin: int, hist_ids,
+                                hist_offsets, params: NcbSamplerParams, records,
+                                stream=None) -> None:
+        """Records of columns [col_begin, col_begin + width) of every row;
+        `logits_shard` is [rows, width] (row stride from the tensor)."""
+        rows, width = int(logits_shard.shape[0]), int(logits_shard.shape[1])
+        ld = int(logits_shard.stride(0)) if rows > 1 else width
+        check(self._lib.ncb_vocab_shard_candidates_device(
+            self._h, _ptr(logits_shard), rows, int(vocab), int(col_begin), int(col_begin) + width,
+            ld, _ptr(hist_ids), _ptr(hist_offsets), ctypes.byref(params), _ptr(records),
+            _stream_ptr(stream)), "ncb_vocab_shard_candidates_device")
+
+    def shard_merge_device(self, records, shards: int, rows: int, vocab: int, uniforms,
+                           params: NcbSamplerParams, tokens, flags=None, stream=None) -> None:
+        """Tokens from the gathered records ([shards][rows], column order)."""
+        check(self._lib.ncb_vocab_shard_merge_device(
+            self._h, _ptr(records), int(shards), int(rows), int(vocab), _ptr(uniforms),
+            ctypes.byref(params), _ptr(tokens), _ptr(flags), _stream_ptr(stream)),
+            "ncb_vocab_shard_merge_device")
+
     # ---- LogitsProcessor (in place, device tensors) ----------------------
     def repetition_penalty_(self, logits, hist_ids, hist_offsets, penalty, stream=None):
         check(self._lib.ncb_logits_repetition_penalty_device(

@@ -1,0 +1,118 @@
+"""Sampling over the GPUs of one node, one process per GPU.
+
+TokenSampler.SampleNext (Neuraval/Generation/TokenSampler.cs:10-143) treats
+every row on its own, so a batch splits two ways:
+  - by rows (`row_range`): each GPU samples its rows with the single-GPU entry
+    point; no data crosses GPUs (an optional all-gather of the B int32 tokens);
+  - by vocabulary (`vocab_range`, `VocabShardedSampler`): each GPU holds its
+    columns of every row (a tensor-parallel LM head), reduces them to one
+    fixed-size record per row, the records of all GPUs are all-gathered in
+    column order (one NCCL collective of rows x 1040 bytes per GPU), and every
+    GPU merges them into the same tokens the whole rows give on one GPU.
+torch.distributed provides the process group and the collective; NCCL on GPUs,
+gloo for the host-side tests.
+"""
+from __future__ import annotations
+
+import contextlib
+from typing import Sequence
+
+
+def row_range(rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous rows of `rank`; sizes differ by at most one."""
+    if world <= 0 or not 0 <= rank < world or rows < 0:
+        raise ValueError("bad rows/world/rank")
+    base, extra = divmod(rows, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def vocab_range(vocab: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous columns of `rank`: ceil(vocab / world) rounded up to a multiple
+    of 4 per shard (16-byte aligned column offsets), the last shard shorter.
+    A shard may be empty only when vocab < 4 * world."""
+    if world <= 0 or not 0 <= rank < world or vocab <= 0:
+        raise ValueError("bad vocab/world/rank")
+    step = -(-vocab // world)
+    step = (step + 3) // 4 * 4
+    lo = min(rank * step, vocab)
+    return lo, min(lo + step, vocab)
+
+
+def gather_records(local, group=None):
+    """All-gather a [rows, words] tensor from every rank into [world, rows, words],
+    rank order (= column order for vocabulary shards)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    local = local.contiguous()
+    out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), local, group=group)
+    return out
+
+
+def max_over_ranks(values: Sequence[float], device=None, group=None) -> list[float]:
+    """Element-wise maximum of `values` over the ranks (timings: the slowest rank)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return [float(x) for x in t.cpu()]
+
+
+class VocabShardedSampler:
+    """Batched SampleNext over a vocabulary split in `vocab_range` shards, one per rank.
+
+    Every rank calls `sample` with its [rows, width] columns; every rank gets
+    all rows' tokens. Served: greedy rows and top-k <= 64 (the library returns
+    NCB_ERROR_CAPACITY for other options).
+    """
+
+    def __init__(self, sampler, vocab: int, group=None):
+        import torch.distributed as dist
+        self.sampler = sampler
+        self.vocab = int(vocab)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.col_begin, self.col_end = vocab_range(self.vocab, self.world, self.rank)
+        self.rec_words = sampler.shard_record_bytes // 4
+        self._local = None
+
+    @property
+    def width(self) -> int:
+        return self.col_end - self.col_begin
+
+    def _records(self, rows: int, device):
+        import torch
+        if self._local is None or self._local.shape[0] < rows or self._local.device != device:
+            self._local = torch.empty((rows, self.rec_words), dtype=torch.int32, device=device)
+        return self._local[:rows]
+
+    def sample(self, logits_shard, hist_ids, hist_offsets, uniforms, params, tokens,
+               flags=None, stream=None) -> None:
+        """Asynchronous on `stream` (default: the current stream); the all-gather
+        is ordered after the candidate kernel and before the merge."""
+        import torch
+        rows, width = int(logits_shard.shape[0]), int(logits_shard.shape[1])
+        if width != self.width:
+            raise ValueError(f"rank {self.rank} holds columns [{self.col_begin}, {self.col_end}),"
+                             f" got {width}")
+        dev = logits_shard.device
+        ctx = torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+        with ctx:
+            cur = torch.cuda.current_stream(dev)
+            local = self._records(rows, dev)
+            if width > 0:
+                self.sampler.shard_candidates_device(logits_shard, self.vocab, self.col_begin,
+                                                     hist_ids, hist_offsets, params, local, cur)
+            else:
+                local.zero_()  # an empty shard: no candidates, no state
+            gathered = gather_records(local, self.group)
+            self.sampler.shard_merge_device(gathered, self.world, rows, self.vocab, uniforms,
+                                            params, tokens, flags, cur)
+
