@@ -16,6 +16,7 @@ cannot run here (no .NET runtime), so its C restatement (oracle/) stands in.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import re
@@ -33,6 +34,7 @@ METRIC = "sampled rows/sec at B×V=256×128256 fp32; achieved HBM GB/s vs B200 p
 UNIT = "rows/s"
 FALLBACK_HBM_GBS = 6650.0
 NBUF = 4  # input copies rotated across steps: 4 x 132 MB > 126 MB L2
+L2_BYTES = 126 * 1024 * 1024
 
 
 def parse():
@@ -43,6 +45,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="zipf_ranked", choices=["zipf_ranked", "vocab_sharded"],
+                    help="zipf_ranked: the headline (rows shard over GPUs); vocab_sharded: "
+                         "128 x 262144, vocabulary split over GPUs")
     return ap.parse_args()
 
 
@@ -53,9 +58,11 @@ def dist_env():
     return rank, world, local
 
 
-def workload():
+def workload(rank=0):
+    """The headline batch; rank r > 0 of a multi-GPU run gets its own rows
+    (same generator, another seed)."""
     from neuraval_b200 import workloads
-    return workloads.zipf_ranked()
+    return workloads.zipf_ranked() if rank == 0 else workloads.zipf_ranked(seed=3 + 1000 * rank)
 
 
 def config_of(wl, extra=None):
@@ -216,8 +223,6 @@ def main():
         return run_reference(args, rank, world)
 
     import torch
-    from neuraval_b200 import native, workloads
-    from neuraval_b200.sampler import CudaTokenSampler
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -226,11 +231,32 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    wl = workload()
+    try:
+        if args.workload == "vocab_sharded":
+            out = run_vocab_sharded(args, rank, world, dev)
+        else:
+            out = run_rows(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_rows(args, rank, world, dev):
+    """The headline: every rank samples its own 256-row batch (rows shard with
+    no exchange), timed as one replay of a CUDA graph holding the K steps."""
+    import torch
+    from neuraval_b200 import native, sharding, workloads
+    from neuraval_b200.sampler import CudaTokenSampler
+
+    wl = workload(rank)
     B, V = wl["logits"].shape
     H = int(wl["hist_offsets"][-1] // B)
     params = native.make_params(**wl["params"])
-    sampler = CudaTokenSampler(device=local, max_rows=B, max_vocab=V, max_history=H)
+    sampler = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=V, max_history=H)
 
     bufs = []
     for i in range(NBUF):
@@ -243,7 +269,6 @@ def main():
     u = torch.from_numpy(wl["uniforms"]).to(dev)
     tokens = torch.empty(B, dtype=torch.int32, device=dev)
     flags = torch.empty(B, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
     def step(i, stream):
         sampler.sample_rows_device(bufs[i % NBUF], hist, offs, u, params, tokens, flags,
@@ -278,7 +303,7 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev.index)
     with clocks:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
@@ -286,12 +311,8 @@ def main():
         graph.replay()
         t_end.record(cur)
         torch.cuda.synchronize()
-    total_ms = t_start.elapsed_time(t_end)
+    total_ms, eager_ms = sharding.max_over_ranks([t_start.elapsed_time(t_end), eager_ms], dev)
     per_launch_ms = total_ms / args.steps
-    if world > 1:
-        t = torch.tensor([total_ms, per_launch_ms, eager_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms, per_launch_ms, eager_ms = float(t[0]), float(t[1]), float(t[2])
     value = world * B * args.steps / (total_ms / 1e3)
     del graph
 
@@ -309,11 +330,7 @@ def main():
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
             sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
-        e2e_s = time.perf_counter() - t0
-        if world > 1:
-            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            e2e_s = float(t[0])
+        (e2e_s,) = sharding.max_over_ranks([time.perf_counter() - t0], dev)
         e2e = {"value": world * B * args.e2e_steps / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": int(h_logits.nbytes + h_hist.nbytes + h_offs.nbytes +
                                          h_u.nbytes),
@@ -321,6 +338,7 @@ def main():
                "api": "ncb_sample_rows (host arrays; copies in, samples, synchronises, "
                       "copies out)"}
 
+    out = None
     if rank == 0:
         peak, peak_kind = measured_peak()
         bytes_per_launch = B * workloads.bytes_per_row(V, H)
@@ -329,7 +347,8 @@ def main():
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
-               "config": config_of(wl, {"parallelism": f"rows sharded, {world} GPU(s), no exchange"}),
+               "config": config_of(wl, {"parallelism": f"rows sharded, {world} GPU(s) x {B} rows"
+                                                       ", no exchange"}),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "peak_source": peak_kind,
                             "traffic": profiled_traffic(),
@@ -338,18 +357,146 @@ def main():
                "e2e": e2e,
                "gpu_launches": 2 * args.steps,
                "eager_value": world * B * args.steps / (eager_ms / 1e3),
-               "timing": "CUDA events around one replay of a CUDA graph holding the K steps",
+               "timing": "CUDA events around one replay of a CUDA graph holding the K steps; "
+                         "max over ranks",
                "clocks": clocks.summary()}
         if world == 1 and args.cpu_seconds > 0:
             v, cores, sample, one = cpu_baseline(wl, args.cpu_seconds)
             out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                                    "sample": sample, "single_thread_value": one}
-        print(json.dumps(out), flush=True)
     sampler.close()
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
-    return 0
+    return out
+
+
+def run_vocab_sharded(args, rank, world, dev):
+    """The 128 x 262144 batch (top-k 64) with its vocabulary split over the ranks:
+    per step, the shard candidate kernel, one NCCL all-gather of the records and
+    the merge kernel on every rank. Total work is fixed (strong scaling). The
+    K steps are captured in one CUDA graph (the all-gather included) and
+    replayed; each part is also timed alone the same way."""
+    import torch
+    from neuraval_b200 import native, sharding, workloads
+    from neuraval_b200.sampler import CudaTokenSampler
+
+    wl = workloads.vocab_sharded()
+    B, V = wl["logits"].shape
+    H = int(wl["hist_offsets"][-1] // B)
+    params = native.make_params(**wl["params"])
+    lo, hi = sharding.vocab_range(V, world, rank)
+    width = hi - lo
+    sampler = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=max(width, 1),
+                               max_history=H)
+    shard = torch.from_numpy(np.ascontiguousarray(wl["logits"][:, lo:hi]))
+    # rotated copies of the shard: a copy is read again only after twice the L2
+    # capacity has streamed through
+    nbuf = min(32, max(2, -(-2 * L2_BYTES // max(1, B * width * 4))))
+    bufs = [shard.to(dev).roll(i, dims=0).contiguous() for i in range(nbuf)]
+    hist = torch.from_numpy(wl["hist_ids"]).to(dev)
+    offs = torch.from_numpy(wl["hist_offsets"]).to(dev)
+    u = torch.from_numpy(wl["uniforms"]).to(dev)
+    tokens = torch.empty(B, dtype=torch.int32, device=dev)
+    flags = torch.empty(B, dtype=torch.int32, device=dev)
+    words = sampler.shard_record_bytes // 4
+    local = torch.zeros((B, words), dtype=torch.int32, device=dev)
+    gathered = torch.zeros((world, B, words), dtype=torch.int32, device=dev)
+
+    def candidates(i):
+        sampler.shard_candidates_device(bufs[i % nbuf], V, lo, hist, offs, params, local,
+                                        torch.cuda.current_stream(dev))
+
+    def exchange(i):
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(gathered, local)
+        else:
+            gathered[0].copy_(local)
+
+    def merge(i):
+        sampler.shard_merge_device(gathered, world, B, V, u, params, tokens, flags,
+                                   torch.cuda.current_stream(dev))
+
+    def full(i):
+        candidates(i)
+        exchange(i)
+        merge(i)
+
+    cur = torch.cuda.current_stream(dev)
+    for i in range(max(3, args.warmup)):
+        full(i)
+    torch.cuda.synchronize()
+
+    def timed(fn, clocks=None):
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(cur)
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(args.steps):
+                    fn(i)
+        torch.cuda.synchronize()
+        graph.replay()  # one untimed replay
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with (clocks if clocks is not None else contextlib.nullcontext()):
+            t0.record(cur)
+            graph.replay()
+            t1.record(cur)
+            torch.cuda.synchronize()
+        del graph  # graphs holding NCCL calls go before the process group
+        return t0.elapsed_time(t1)
+
+    clocks = ClockSampler(dev.index)
+    total_ms = timed(full, clocks)
+    parts = [timed(candidates), timed(exchange), timed(merge)]
+    total_ms, *parts = sharding.max_over_ranks([total_ms] + parts, dev)
+    # the sampled tokens equal the single-GPU sampler's on the whole rows
+    ok = True
+    full(0)  # every rank: the step holds a collective
+    torch.cuda.synchronize()
+    if rank == 0:
+        ref_s = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=V, max_history=H)
+        full_logits = torch.from_numpy(wl["logits"]).to(dev)
+        rt = torch.empty_like(tokens)
+        rf = torch.empty_like(flags)
+        ref_s.sample_rows_device(full_logits, hist, offs, u, params, rt, rf)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(rt, tokens) and torch.equal(rf, flags))
+        ref_s.close()
+        del full_logits
+    out = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        per_gpu_bytes = B * (4 * width + 4 * H + 8)
+        per_step_s = total_ms / args.steps / 1e3
+        out = {"metric": "sampled rows/sec, vocabulary split over GPUs", "value":
+               B * args.steps / (total_ms / 1e3), "unit": UNIT, "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
+               "config": config_of(wl, {"parallelism": f"vocabulary sharded over {world} GPU(s);"
+                                                       " records all-gathered (NCCL)",
+                                        "l2": f"{nbuf} rotated copies of each shard",
+                                        "shard_columns": width,
+                                        "record_bytes_per_rank": B * sampler.shard_record_bytes}),
+               "parts_us_per_step": {"candidates": parts[0] / args.steps * 1e3,
+                                     "all_gather": parts[1] / args.steps * 1e3,
+                                     "merge": parts[2] / args.steps * 1e3},
+               "tokens_match_single_gpu": ok,
+               "roofline": {"bound": "hbm", "achieved": per_gpu_bytes / per_step_s / 1e9,
+                            "peak": peak, "unit": "GB/s",
+                            "frac": per_gpu_bytes / per_step_s / 1e9 / peak,
+                            "peak_source": peak_kind, "traffic": None,
+                            "kernel": "shard candidate kernel + all-gather + merge, per step",
+                            "algorithmic_bytes_per_launch": per_gpu_bytes},
+               "e2e": None,
+               "gpu_launches": 2 * args.steps,  # candidates + merge (NCCL's kernel not counted)
+               "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
+                         "(all-gather included); max over ranks",
+               "clocks": clocks.summary()}
+    sampler.close()
+    return out
 
 
 if __name__ == "__main__":

@@ -330,7 +330,7 @@ __device__ uint32_t cta_kth_largest_key(GetA getA, int na, GetB getB, int nb, in
 
 // ---------------------------------------------------------------------------
 // Bulk-async (TMA engine) copies global -> shared with mbarrier completion.
-// No cluster multicast anywhere in this library.
+// Every copy lands in the issuing CTA's own shared memory, from this GPU's memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
