@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
 
 // Warp-aggregated append of one optional candidate per lane. All 32 lanes call.
 __device__ __forceinline__ void warp_append(bool pred, float v, int id, float* cv, int* cid,
-                                            int* s_count, int* s_overflow) {
+                                            int* s_count, int* s_overflow, int cap = TK_CAPB) {
   const unsigned b = __ballot_sync(0xffffffffu, pred);
   if (b == 0u) return;
   const int lane = threadIdx.x & 31;
@@ -247,7 +247,7 @@ __device__ __forceinline__ void warp_append(bool pred, float v, int id, float* c
   base = __shfl_sync(0xffffffffu, base, leader);
   if (pred) {
     const int slot = base + __popc(b & ((1u << lane) - 1u));
-    if (slot < TK_CAPB) {
+    if (slot < cap) {
       cv[slot] = v;
       cid[slot] = id;
     } else {

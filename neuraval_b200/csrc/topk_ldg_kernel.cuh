@@ -120,6 +120,10 @@ __device__ uint32_t cta_kth_largest_warphist(const uint32_t (&keys)[N], int k, i
 
 
 constexpr int TL_NB = 1024;   // linear bins of the selection histograms (2 per thread)
+constexpr int TL_GCAP = 1024;  // candidates gathered by the final select (lower half of cv/cid)
+constexpr int TL_BINCAP = 256; // values of the K-th value's bin
+constexpr int TL_TOPW = 16;    // keys per warp in the final lists (16 x 16 = 256)
+constexpr int TL_LISTV = 512;  // float offset in cv of the lists' value keys (after 256 keys)
 
 // k-th largest of the values held N per thread (valid[j] marks real values;
 // -inf, NaN and +inf must not be marked), via one histogram of TL_NB linear
@@ -284,8 +288,13 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
 
   __shared__ int s_hn, s_nonfinite, s_overflow, s_count, s_last, s_ovf, s_tot;
   __shared__ int s_wn[TL_WARPS];
+  __shared__ float s_wtheta[TL_WARPS], s_wmax[TL_WARPS];
+  __shared__ int s_bstar, s_above, s_nbin, s_mode;
+  __shared__ float s_kth;
+  __shared__ uint64_t s_xkey, s_maxkey;
+  __shared__ int s_flags2, s_c;
   __shared__ int s_sh[2];
-  __shared__ float s_theta0;
+  __shared__ float s_theta0, s_u;
   __shared__ uint32_t s_state;
   __shared__ Penalty s_pen;
 
@@ -314,6 +323,8 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     const int q = tid + u * TL_THREADS;
     x0[u] = q < n4 ? __ldcs(body + q) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+
+  if (!kShard && tid == 0) s_u = a.uniforms[row];  // read by the finish
 
   Penalty P;
   const bool hist_ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
@@ -465,7 +476,57 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   }
   if (nonfinite) s_nonfinite = 1;
   if (tie_ovf && lane == 0) s_overflow = 1;
-  if (lane == 0) s_wn[warp] = count;
+  // the final select's histogram range: [largest warp threshold, largest
+  // buffered value]; its bins (upper half of cv) are free during the stream
+  uint32_t* bins = reinterpret_cast<uint32_t*>(cv + TL_GCAP);  // [TL_NB]
+  {
+    float wmx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < TW_WCAP / 32; ++r)
+      if (r * 32 + lane < count) wmx = fmaxf(wmx, wv[r * 32 + lane]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wmx = fmaxf(wmx, __shfl_xor_sync(0xffffffffu, wmx, o));
+    if (lane == 0) {
+      s_wn[warp] = count;
+      s_wtheta[warp] = theta;  // a lower bound of the segment's K-th value
+      s_wmax[warp] = wmx;
+    }
+    // the warp's TL_TOPW largest keys, descending, to the list area (cv[0..)):
+    // each lane sorts its 4 entries, then rounds of warp max (redux) pop heads
+    uint64_t k[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = r * 32 + lane;
+      k[r] = i < count ? cand_key(wv[i], wi[i]) : 0ull;
+    }
+    sort4_desc(k);
+    uint64_t mine = 0ull;
+#pragma unroll
+    for (int t = 0; t < TL_TOPW; ++t) {
+      const uint32_t hv = __reduce_max_sync(0xffffffffu, (uint32_t)(k[0] >> 32));
+      const bool eq = (uint32_t)(k[0] >> 32) == hv;
+      const uint32_t lv = __reduce_max_sync(0xffffffffu, eq ? (uint32_t)k[0] : 0u);
+      if (lane == t) mine = ((uint64_t)hv << 32) | lv;
+      if (eq && (uint32_t)k[0] == lv && k[0] != 0ull) {
+        k[0] = k[1];
+        k[1] = k[2];
+        k[2] = k[3];
+        k[3] = 0ull;
+      }
+    }
+    if (lane < TL_TOPW) {
+      reinterpret_cast<uint64_t*>(cv)[warp * TL_TOPW + lane] = mine;
+      reinterpret_cast<uint32_t*>(cv + TL_LISTV)[warp * TL_TOPW + lane] = (uint32_t)(mine >> 32);
+    }
+    if (tid == 0) {
+      s_xkey = 0ull;
+      s_maxkey = 0ull;
+      s_flags2 = 0;
+      s_c = 0;
+    }
+#pragma unroll
+    for (int j = lane; j < TL_NB / TL_WARPS; j += 32) bins[warp * (TL_NB / TL_WARPS) + j] = 0u;
+  }
   __syncwarp();
   __syncthreads();
 
@@ -476,7 +537,239 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   if (s_overflow) state |= RSTATE_OVERFLOW;
   int m = 0;
   float kth = -INFINITY;  // the segment's K-th largest value
+
+  // ---- exact K-th value over the warp buffers ---------------------------------
+  // One linear histogram of the buffered values >= lo (the largest warp
+  // threshold, a lower bound of the K-th value) over [lo, hi]; warp 0 finds
+  // the bin b* holding the K-th value; one pass appends every value of the
+  // bins above b* (all candidates) and collects bin b*; warp 0 ranks bin b*
+  // and appends its values >= the K-th. Unusual inputs (no finite lower bound,
+  // a crowded bin b*, too many candidates) take the general select below.
+  bool done = false;
+  // One-CTA rows: every warp published its 16 largest keys (sorted). Each key
+  // gets its rank among all 256 by binary searches in the other lists; the
+  // key of rank K-1 is x. No warp holds more than its list above x unless its
+  // 16th key is >= x, so then every candidate (value >= x) is a list key and
+  // its rank is its place in the sorted order: the candidates are scattered
+  // to their places with their weights, and warp 0 finishes. Otherwise (a
+  // full list, too many ties, too few keys) the selects below run.
+  if (S == 1 && state == 0u) {
+    const uint64_t* lists = reinterpret_cast<const uint64_t*>(cv);  // [TL_WARPS][TL_TOPW]
+    const uint32_t* lval = reinterpret_cast<const uint32_t*>(cv + TL_LISTV);  // value keys
+    uint64_t* sk = reinterpret_cast<uint64_t*>(cid);                // [64] keys by rank
+    float* sw = reinterpret_cast<float*>(cid + 128);                // [64] weights by rank
+    // lb: every warp holds >= kq+1 keys >= its (kq+1)-th key and
+    // TL_WARPS*(kq+1) >= K, so the smallest of those is a lower bound of the
+    // K-th value; keys below it need no rank
+    const int kq = (K + TL_WARPS - 1) / TL_WARPS - 1;
+    uint32_t lb = lval[(lane & (TL_WARPS - 1)) * TL_TOPW + kq];
+#pragma unroll
+    for (int o = TL_WARPS / 2; o > 0; o >>= 1) lb = min(lb, __shfl_xor_sync(0xffffffffu, lb, o));
+    const int j = lane & (TL_TOPW - 1), half = lane >> 4;
+    const uint64_t key = lists[warp * TL_TOPW + j];
+    const uint32_t vk = (uint32_t)(key >> 32);
+    int cnt = 0;
+    if (key != 0ull && vk >= lb) {
+#pragma unroll
+      for (int t = 0; t < TL_WARPS / 2; ++t) {
+        const int l = half * (TL_WARPS / 2) + t;
+        if (l == warp) continue;  // within its own list a key's rank is its place j
+        const uint32_t* L = lval + l * TL_TOPW;
+        int pos = 0;  // values of list l greater than vk (a sorted prefix)
+#pragma unroll
+        for (int step = TL_TOPW / 2; step > 0; step >>= 1)
+          if (L[pos + step - 1] > vk) pos += step;
+        pos += L[pos] > vk ? 1 : 0;
+        cnt += pos;
+        // equal values rank by id: count those with a larger full key
+        for (int q = pos; q < TL_TOPW && L[q] == vk; ++q) cnt += lists[l * TL_TOPW + q] > key;
+      }
+    }
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, 16);
+    const int rank = j + cnt;
+    if (half == 0 && key != 0ull && vk >= lb) {
+      if (rank == K - 1) s_xkey = key;
+      if (rank == 0) s_maxkey = key;
+    }
+    __syncthreads();
+    const uint64_t x = s_xkey;
+    const float vmax = cand_val(s_maxkey);
+    if (x != 0ull && vmax > -INFINITY) {
+      const uint32_t xv = (uint32_t)(x >> 32);
+      if (lane == 0) {
+        const uint64_t last = lists[warp * TL_TOPW + TL_TOPW - 1];
+        if (last != 0ull && (uint32_t)(last >> 32) >= xv) atomicOr(&s_flags2, 1);  // full list
+      }
+      if (half == 0 && key != 0ull && vk >= lb && vk >= xv) {
+        if (rank < 64) {
+          bool slow = false;
+          sk[rank] = key;
+          sw[rank] = exp_cr(__fsub_rn(cand_val(key), vmax), slow);
+          if (slow) atomicOr(&s_flags2, 4);
+        } else {
+          atomicOr(&s_flags2, 2);  // more than 64 candidates
+        }
+        atomicAdd(&s_c, 1);
+      }
+    }
+    __syncthreads();
+    if (x != 0ull && vmax > -INFINITY && (s_flags2 & 3) == 0) {
+      if (warp == 0) {
+        const int c = s_c;
+        const uint64_t k0 = lane < c ? sk[lane] : 0ull;
+        const uint64_t k1 = lane + 32 < c ? sk[lane + 32] : 0ull;
+        if constexpr (kShard) {
+          uint32_t* rec = a.shard_out + (size_t)row * VS_REC_WORDS;
+          float* rv = vs_values(rec);
+          int32_t* ri = vs_ids(rec);
+          if (lane < c) {
+            rv[lane] = cand_val(k0);
+            ri[lane] = cand_id(k0);
+          }
+          if (lane + 32 < c) {
+            rv[lane + 32] = cand_val(k1);
+            ri[lane + 32] = cand_id(k1);
+          }
+          if (lane == 0) {
+            rec[0] = (uint32_t)c;
+            rec[1] = 0u;
+            rec[2] = __float_as_uint(cand_val(x));
+            rec[3] = (uint32_t)c;
+          }
+        } else {
+          finish_weights_warp(a, row, k0, k1, c, sw, reinterpret_cast<float*>(work),
+                              (s_flags2 & 4) != 0, s_u);
+        }
+      }
+      return;
+    }
+  }
   if (state == 0u) {
+    float lo = s_wtheta[lane & (TL_WARPS - 1)], hi = s_wmax[lane & (TL_WARPS - 1)];
+#pragma unroll
+    for (int o = TL_WARPS / 2; o > 0; o >>= 1) {
+      lo = fmaxf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (lo > -INFINITY && hi > lo) {
+      const float sc = __fdiv_rn((float)TL_NB, __fsub_rn(hi, lo));
+      auto bin_of = [&](float x) {
+        const int b = (int)__fmul_rn(__fsub_rn(hi, x), sc);  // larger x -> smaller bin
+        return b < TL_NB - 1 ? b : TL_NB - 1;
+      };
+      float fv[TW_WCAP / 32];
+      bool fok[TW_WCAP / 32];
+#pragma unroll
+      for (int r = 0; r < TW_WCAP / 32; ++r) {
+        const int i = tid + r * TL_THREADS;  // flattened [W][WCAP]
+        const int w = i / TW_WCAP, e = i % TW_WCAP;
+        fv[r] = e < s_wn[w] ? wvall[i] : -INFINITY;
+        fok[r] = fv[r] >= lo;
+        if (fok[r]) atomicAdd(&bins[bin_of(fv[r])], 1u);
+      }
+      if (tid == 0) {
+        s_count = 0;
+        s_ovf = 0;
+        s_nbin = 0;
+        s_bstar = -1;
+        s_mode = 0;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // lane l owns bins [32l, 32l+32): totals, scan, then the crossing lane
+        constexpr int PER = TL_NB / 32;
+        int c = 0;
+#pragma unroll 8
+        for (int j = 0; j < PER; ++j) c += (int)bins[lane * PER + j];
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const int excl = incl - c;
+        if (excl < K && K <= incl) {
+          int run = excl, j = 0;
+          for (; j < PER; ++j) {
+            const int cb = (int)bins[lane * PER + j];
+            if (run + cb >= K) break;
+            run += cb;
+          }
+          s_bstar = lane * PER + j;
+          s_above = run;
+        }
+      }
+      __syncthreads();
+      const int bstar = s_bstar;
+      if (bstar >= 0) {
+        float* binv = reinterpret_cast<float*>(cid + TL_GCAP);  // [TL_BINCAP]
+        int* bini = cid + TL_GCAP + TL_BINCAP;                   // [TL_BINCAP]
+#pragma unroll
+        for (int r = 0; r < TW_WCAP / 32; ++r) {
+          const int i = tid + r * TL_THREADS;
+          const int b = fok[r] ? bin_of(fv[r]) : TL_NB;
+          const bool above = b < bstar;
+          warp_append(above, fv[r], above ? wiall[i] : 0, cv, cid, &s_count, &s_ovf, TL_GCAP);
+          if (b == bstar) {
+            const int slot = atomicAdd(&s_nbin, 1);
+            if (slot < TL_BINCAP) {
+              binv[slot] = fv[r];
+              bini[slot] = wiall[i];
+            }
+          }
+        }
+        __syncthreads();
+        if (warp == 0) {
+          const int nb = s_nbin;
+          const int rk = K - s_above;  // rank of the K-th value inside bin b* (1-based)
+          if (nb <= TL_BINCAP && !s_ovf) {
+            // the K-th value: the bin entry x with #(> x) < rk <= #(>= x)
+            float T = -INFINITY;
+            for (int j0 = 0; j0 < nb; j0 += 32) {
+              const int j = j0 + lane;
+              const float x = j < nb ? binv[j] : -INFINITY;
+              int gt = 0, ge = 0;
+              for (int t = 0; t < nb; ++t) {
+                const float y = binv[t];
+                gt += y > x;
+                ge += y >= x;
+              }
+              const bool hit = j < nb && gt < rk && rk <= ge;
+              const unsigned hb = __ballot_sync(0xffffffffu, hit);
+              if (hb) T = __shfl_sync(0xffffffffu, x, __ffs(hb) - 1);
+            }
+            // bin b* values >= T join the candidates
+            for (int j0 = 0; j0 < nb; j0 += 32) {
+              const int j = j0 + lane;
+              const bool ok = j < nb && binv[j] >= T;
+              warp_append(ok, ok ? binv[j] : 0.f, ok ? bini[j] : 0, cv, cid, &s_count, &s_ovf,
+                          TL_GCAP);
+            }
+            __syncwarp();
+            const int mm = s_count;
+            if (!s_ovf) {
+              if (!kShard && S == 1 && mm <= 64) {
+                finish_row_warp(a, row, cv, cid, mm, reinterpret_cast<float*>(work), false, s_u);
+                if (lane == 0) s_mode = 2;  // finished
+              } else if (lane == 0) {
+                s_mode = 1;  // candidates ready
+                s_kth = T;
+              }
+            }
+          }
+        }
+        __syncthreads();
+        if (s_mode == 2) return;
+        if (s_mode == 1) {
+          done = true;
+          kth = s_kth;
+          m = s_count;
+        }
+      }
+    }
+  }
+
+  if (state == 0u && !done) {
     // exact K-th largest over the warp buffers (finite values; -inf entries
     // are below any finite K-th value and are all kept when it is -inf)
     float fv[TW_WCAP / 32];

@@ -134,42 +134,76 @@ __device__ __forceinline__ void warp_append_reg(bool c, float c_v, int c_id, flo
   count += __popc(b);
 }
 
-// Finishing stage by one warp for m <= 64 candidates (TokenSampler.cs:95-132).
-// `wsm` holds 128 floats of shared memory. Only warp 0 calls.
-__device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const float* cv,
-                                            const int* cid, int m, float* wsm,
-                                            bool presorted = false) {
+// Sorts 4 keys of one thread descending (5 compare-exchanges).
+__device__ __forceinline__ void sort4_desc(uint64_t (&k)[4]) {
+  auto cx = [](uint64_t& a, uint64_t& b) {
+    if (a < b) {
+      const uint64_t t = a;
+      a = b;
+      b = t;
+    }
+  };
+  cx(k[0], k[1]);
+  cx(k[2], k[3]);
+  cx(k[0], k[2]);
+  cx(k[1], k[3]);
+  cx(k[1], k[2]);
+}
+
+// Warp bitonic sort, descending, of 64 keys held 2 per lane at index r*32+lane.
+__device__ __forceinline__ void warp_sort64_desc(uint64_t& k0, uint64_t& k1) {
   const int lane = threadIdx.x & 31;
-  uint64_t k[2];
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int i = r * 32 + lane;
-    k[r] = i < m ? cand_key(cv[i], cid[i]) : 0ull;
-  }
-  // bitonic sort of 64 keys, descending (skipped for an already sorted input)
-#pragma unroll
-  for (int size = 2; size <= (presorted ? 1 : 64); size <<= 1) {
+  for (int size = 2; size <= 64; size <<= 1) {
 #pragma unroll
     for (int j = size >> 1; j > 0; j >>= 1) {
+      if (j == 32) {
+        // size 64: one descending block, k0 holds the lower indices
+        if (k0 < k1) {
+          const uint64_t t = k0;
+          k0 = k1;
+          k1 = t;
+        }
+      } else {
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int i = r * 32 + lane;
-        const bool down = (i & size) == 0;
-        if (j >= 32) {
-          if (r == 0) {
-            const uint64_t x = k[0], y = k[1];
-            const bool sw = down ? (x < y) : (x > y);
-            if (sw) { k[0] = y; k[1] = x; }
-          }
-        } else {
-          const uint64_t o = __shfl_xor_sync(0xffffffffu, k[r], j);
+        for (int r = 0; r < 2; ++r) {
+          uint64_t& k = r == 0 ? k0 : k1;
+          const int i = r * 32 + lane;
+          const bool down = (i & size) == 0;
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, k, j);
           const bool lower = (lane & j) == 0;
-          const uint64_t mx = k[r] > o ? k[r] : o, mn = k[r] > o ? o : k[r];
-          k[r] = (lower == down) ? mx : mn;
+          const uint64_t mx = k > o ? k : o, mn = k > o ? o : k;
+          k = (lower == down) ? mx : mn;
         }
       }
     }
   }
+}
+
+__device__ void finish_keys_warp(const SampleArgs& a, int row, uint64_t k0, uint64_t k1, int m,
+                                 float* wsm, float u);
+__device__ void finish_weights_warp(const SampleArgs& a, int row, uint64_t k0, uint64_t k1, int m,
+                                    const float* __restrict__ w, float* __restrict__ S,
+                                    bool any_slow, float u);
+
+// Finishing stage by one warp for m <= 64 candidates (TokenSampler.cs:95-132).
+// `wsm` holds 128 floats of shared memory. Only warp 0 calls.
+__device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const float* cv,
+                                            const int* cid, int m, float* wsm,
+                                            bool presorted = false, float u = -1.0f) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k0 = lane < m ? cand_key(cv[lane], cid[lane]) : 0ull;
+  uint64_t k1 = lane + 32 < m ? cand_key(cv[lane + 32], cid[lane + 32]) : 0ull;
+  if (!presorted) warp_sort64_desc(k0, k1);
+  finish_keys_warp(a, row, k0, k1, m, wsm, u >= 0.0f ? u : a.uniforms[row]);
+}
+
+// The same from keys already sorted descending (index r*32+lane in k0/k1; the
+// first m are the candidates) and the row's uniform u.
+__device__ __noinline__ void finish_keys_warp(const SampleArgs& a, int row, uint64_t k0,
+                                             uint64_t k1, int m, float* wsm, float u) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k[2] = {k0, k1};
   const float vmax = cand_val(__shfl_sync(0xffffffffu, k[0], 0));
   float* w = wsm;        // [64]
   float* S = wsm + 64;   // [64]
@@ -188,12 +222,33 @@ __device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const
   }
   const bool any_slow = __any_sync(0xffffffffu, slow);
   __syncwarp();
-  // sequential fp32 sums in sorted order (lane 0; the loads run ahead of
-  // the dependent adds), then the cutoff and draw searches by ballot
+  finish_weights_warp(a, row, k0, k1, m, w, S, any_slow, u);
+}
+
+// The rest of the finish once the weights w[i] = exp(v_i - max) of the m
+// sorted candidates are in shared memory (`S`: 64 floats of scratch).
+__device__ __noinline__ void finish_weights_warp(const SampleArgs& a, int row, uint64_t k0,
+                                                uint64_t k1, int m, const float* __restrict__ w,
+                                                float* __restrict__ S, bool any_slow, float u) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k[2] = {k0, k1};
+  // sequential fp32 sums in sorted order (lane 0; w and S do not overlap, so
+  // the loads run ahead of the dependent adds), then the cutoff and draw
+  // searches by ballot
   if (lane == 0) {
     float total = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < m; ++i) {
+    int i = 0;
+    for (; i + 8 <= m; i += 8) {
+      float t[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t[q] = w[i + q];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        total = __fadd_rn(total, t[q]);
+        S[i + q] = total;
+      }
+    }
+    for (; i < m; ++i) {
       total = __fadd_rn(total, w[i]);
       S[i] = total;
     }
@@ -209,7 +264,7 @@ __device__ __noinline__ void finish_row_warp(const SampleArgs& a, int row, const
     cutoff = b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : m);
   }
   const float retained = S[cutoff - 1];
-  const float sample = __fmul_rn(a.uniforms[row], retained);
+  const float sample = __fmul_rn(u, retained);
   int sel;
   {
     const unsigned b0 = __ballot_sync(0xffffffffu, lane < cutoff && sample <= S[lane]);

@@ -67,6 +67,19 @@ def test_zipf_ranked_full_size(gpu_sampler, oracle):
     print("zipf_ranked parity", rep)
 
 
+@pytest.mark.parametrize("mantissa_bits", [7, 3])
+def test_quantised_logits_with_ties(gpu_sampler, oracle, mantissa_bits):
+    # logits of a bf16 model (7 mantissa bits) and coarser: many exactly equal
+    # values around the K-th, across the kernel's warps and at the draw
+    wl = workloads.zipf_ranked(B=64, V=50000, H=256, seed=31)
+    lg = wl["logits"].astype(np.float32)
+    m, e = np.frexp(lg)
+    q = np.float32(2.0 ** (mantissa_bits + 1))
+    wl["logits"] = np.ldexp(np.round(m * q) / q, e).astype(np.float32)
+    rep = full_check(gpu_sampler, oracle, wl, probs=True, label=f"quantised {mantissa_bits}")
+    print("quantised parity", mantissa_bits, rep)
+
+
 def test_zipf_history_nucleus_full_size(gpu_sampler, oracle):
     wl = workloads.zipf_history_nucleus()
     rep = full_check(gpu_sampler, oracle, wl, probs=True, label="zipf_history_nucleus 32x32000")
