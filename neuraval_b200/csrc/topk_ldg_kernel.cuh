@@ -24,6 +24,7 @@
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
 #include "warp_select.cuh"
+#include "rank_select.cuh"
 
 namespace nvs {
 
@@ -553,7 +554,8 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   // its rank is its place in the sorted order: the candidates are scattered
   // to their places with their weights, and warp 0 finishes. Otherwise (a
   // full list, too many ties, too few keys) the selects below run.
-  if (S == 1 && state == 0u) {
+  bool published = false;  // a split row's segment candidates already in scratch
+  if (state == 0u) {
     const uint64_t* lists = reinterpret_cast<const uint64_t*>(cv);  // [TL_WARPS][TL_TOPW]
     const uint32_t* lval = reinterpret_cast<const uint32_t*>(cv + TL_LISTV);  // value keys
     uint64_t* sk = reinterpret_cast<uint64_t*>(cid);                // [64] keys by rank
@@ -613,7 +615,19 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       }
     }
     __syncthreads();
-    if (x != 0ull && vmax > -INFINITY && (s_flags2 & 3) == 0) {
+    if (x != 0ull && vmax > -INFINITY && (s_flags2 & 3) == 0 && S > 1) {
+      // a split row: this segment's candidates (sorted) go to the row's scratch
+      const int c = s_c;
+      const int cta = row * S + split;
+      for (int i = tid; i < c; i += TL_THREADS) {
+        a.s.cand_v[(size_t)cta * TK_CAPB + i] = cand_val(sk[i]);
+        a.s.cand_id[(size_t)cta * TK_CAPB + i] = cand_id(sk[i]);
+      }
+      m = c;
+      kth = cand_val(x);
+      done = true;
+      published = true;
+    } else if (x != 0ull && vmax > -INFINITY && (s_flags2 & 3) == 0) {
       if (warp == 0) {
         const int c = s_c;
         const uint64_t k0 = lane < c ? sk[lane] : 0ull;
@@ -644,7 +658,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       return;
     }
   }
-  if (state == 0u) {
+  if (state == 0u && !done) {
     float lo = s_wtheta[lane & (TL_WARPS - 1)], hi = s_wmax[lane & (TL_WARPS - 1)];
 #pragma unroll
     for (int o = TL_WARPS / 2; o > 0; o >>= 1) {
@@ -816,10 +830,11 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
 
   // ---- multi-CTA rows: publish, the last CTA merges --------------------------
   const int cta = row * S + split;
-  for (int i = tid; i < m; i += TL_THREADS) {
-    a.s.cand_v[(size_t)cta * TK_CAPB + i] = cv[i];
-    a.s.cand_id[(size_t)cta * TK_CAPB + i] = cid[i];
-  }
+  if (!published)
+    for (int i = tid; i < m; i += TL_THREADS) {
+      a.s.cand_v[(size_t)cta * TK_CAPB + i] = cv[i];
+      a.s.cand_id[(size_t)cta * TK_CAPB + i] = cid[i];
+    }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -858,6 +873,44 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       off += n;
     }
     __syncthreads();
+    if (total <= RS_MAX) {
+      // direct ranks over the union: sorted candidates and their weights
+      uint64_t* sk = reinterpret_cast<uint64_t*>(work + 16384);  // [64]
+      float* sw = reinterpret_cast<float*>(work + 16384 + 512);  // [64]
+      float* s64 = sw + 64;                                      // [64]
+      const RankSel rs = cta_rank_select(uv, uid, total, K, reinterpret_cast<uint64_t*>(cv), sk, sw);
+      if (rs.ok) {
+        if (warp == 0) {
+          const uint64_t k0 = lane < rs.c ? sk[lane] : 0ull;
+          const uint64_t k1 = lane + 32 < rs.c ? sk[lane + 32] : 0ull;
+          if constexpr (kShard) {
+            uint32_t* rec = a.shard_out + (size_t)row * VS_REC_WORDS;
+            if (lane < rs.c) {
+              vs_values(rec)[lane] = cand_val(k0);
+              vs_ids(rec)[lane] = cand_id(k0);
+            }
+            if (lane + 32 < rs.c) {
+              vs_values(rec)[lane + 32] = cand_val(k1);
+              vs_ids(rec)[lane + 32] = cand_id(k1);
+            }
+            if (lane == 0) {
+              rec[0] = (uint32_t)rs.c;
+              rec[1] = 0u;
+              rec[2] = __float_as_uint(total < K ? -INFINITY : cand_val(rs.x));
+              rec[3] = (uint32_t)rs.c;
+            }
+          } else {
+            finish_weights_warp(a, row, k0, k1, rs.c, sw, s64, rs.slow, a.uniforms[row]);
+          }
+        }
+        __syncthreads();
+        if (tid == 0) {
+          a.s.rowstate[row] = 0u;
+          a.s.tickets[row] = 0u;
+        }
+        return;
+      }
+    }
     const uint32_t key = cta_kth_largest([&](int i) { return fkey(uv[i]); }, total, K, hist, s_sh);
     mkth = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
     if (tid == 0) {

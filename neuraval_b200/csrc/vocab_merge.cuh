@@ -11,6 +11,7 @@
 #include "shard_record.cuh"
 #include "topk_kernels.cuh"
 #include "warp_select.cuh"
+#include "rank_select.cuh"
 
 namespace nvs {
 
@@ -35,7 +36,8 @@ __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_co
   uint32_t* hist = reinterpret_cast<uint32_t*>(work + VM_WORK);          // [256]
   __shared__ int s_n[VM_MAX_SHARDS], s_off[VM_MAX_SHARDS + 1];
   __shared__ uint32_t s_state, s_kth[VM_MAX_SHARDS];
-  __shared__ int s_sh[2], s_count, s_ovf;
+  __shared__ int s_sh[2], s_count, s_ovf, s_nu;
+  __shared__ float s_lb;
 
   const SampleArgs& a = g.a;
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -99,6 +101,69 @@ __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_co
   // union of the shards' candidates
   float* uv = reinterpret_cast<float*>(work);            // [CAPB]
   int* uid = reinterpret_cast<int*>(uv + TK_CAPB);        // [CAPB]
+  const int K = min(a.p.top_k, a.V);
+  {
+    // Direct ranks over the candidates >= lb, the largest K-th value of a
+    // shard that holds K values (a lower bound of the global K-th value).
+    if (tid == 0) {
+      float lb = -INFINITY;
+      for (int s = 0; s < G; ++s) {
+        const uint32_t* r = rec0 + s * stride;
+        if ((int)r[3] >= K) lb = fmaxf(lb, __uint_as_float(r[2]));
+      }
+      s_lb = lb;
+      s_nu = 0;
+    }
+    __syncthreads();
+    const float lb = s_lb;
+    for (int s = 0; s < G; ++s) {
+      const uint32_t* r = rec0 + s * stride;
+      for (int i = tid; i < s_n[s]; i += VM_THREADS) {
+        const float v = __uint_as_float(r[VS_HDR + i]);
+        if (v >= lb) {
+          const int slot = atomicAdd(&s_nu, 1);
+          if (slot < RS_MAX) {
+            uv[slot] = v;
+            uid[slot] = (int)r[VS_HDR + VS_CAP + i];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const int U = s_nu;
+    if (U <= RS_MAX) {
+      uint64_t* sk = reinterpret_cast<uint64_t*>(work + 16384);  // [64]
+      float* sw = reinterpret_cast<float*>(work + 16384 + 512);  // [64]
+      float* s64 = sw + 64;                                      // [64]
+      const RankSel rs = cta_rank_select(uv, uid, U, K, reinterpret_cast<uint64_t*>(cv), sk, sw);
+      if (rs.ok) {
+        if (tid == 0) {
+          bool cut = false;
+          if (st & VS_OVF_AT_KTH)
+            for (int s = 0; s < G; ++s) {
+              const uint32_t rs_ = rec0[s * stride + 1];
+              if ((rs_ & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == cand_val(rs.x)) cut = true;
+            }
+          s_ovf = cut ? 1 : 0;
+        }
+        __syncthreads();
+        if (s_ovf) {
+          if (tid == 0) {
+            a.tokens[row] = -1;
+            if (a.flags) a.flags[row] = FLAG_TIES_OVERFLOW;
+          }
+          return;
+        }
+        if (warp == 0) {
+          const uint64_t k0 = lane < rs.c ? sk[lane] : 0ull;
+          const uint64_t k1 = lane + 32 < rs.c ? sk[lane + 32] : 0ull;
+          finish_weights_warp(a, row, k0, k1, rs.c, sw, s64, rs.slow, a.uniforms[row]);
+        }
+        return;
+      }
+    }
+    __syncthreads();
+  }
   for (int s = 0; s < G; ++s) {
     const uint32_t* r = rec0 + s * stride;
     const int n = s_n[s], o = s_off[s];
@@ -110,7 +175,6 @@ __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_co
   __syncthreads();
   // fewer than K finite values in the whole row: every finite value is a
   // candidate (key 0 below), the row's -inf values would only add zero weights
-  const int K = min(a.p.top_k, a.V);
   const uint32_t key = cta_kth_largest([&](int i) { return fkey(uv[i]); }, total, K, hist, s_sh);
   const float theta = key <= fkey(-INFINITY) ? -INFINITY : kval(key);
   if (tid == 0) {
