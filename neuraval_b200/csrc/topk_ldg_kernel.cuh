@@ -5,16 +5,20 @@
 //  - every thread streams its float4s with four independent 128-bit loads in
 //    flight (evict-first), so the row is read once with no shared-memory
 //    staging and no barrier in the loop. Per value the loop does one multiply,
-//    one NaN/+inf test and one threshold test; one vote per step of 16 values
-//    decides whether the out-of-line candidate path runs at all;
+//    one NaN/+inf test and one threshold test; one ballot per float4 queues
+//    the float4s that may hold a candidate for a drain outside the loop;
 //  - the first step is also the sample: exact (penalised) values, each
-//    thread's maximum, and the K-th largest of those 512 maxima -- distinct
-//    elements of the segment, so a lower bound of its K-th largest value;
+//    thread's maximum, and a lower bound of the K-th largest of those 512
+//    maxima -- distinct elements of the segment, so a lower bound of its K-th
+//    largest value;
 //  - candidates go to per-warp buffers (ballot + popc); a full buffer is
 //    sorted in registers and cut to its top K plus ties, raising that warp's
 //    threshold;
-//  - one CTA select over the warp buffers gives the segment's K-th largest;
-//    one warp (or the CTA, above 64 candidates) runs the exact finish.
+//  - after the stream every warp publishes its 16 largest keys; ranks by
+//    binary search across those lists give the K-th value and the sorted
+//    candidates directly, weights are computed in parallel and one warp runs
+//    the sequential sums and the draw. Full lists, ties beyond 64 candidates
+//    and split rows fall back to histogram selects over all buffered values.
 // Penalties that can only lower a value (repetition >= 1, frequency and
 // presence >= 0) are applied to candidates only: raw*scale >= theta is a
 // superset test. Other penalties take the exact path for every float4 that
@@ -43,82 +47,6 @@ inline size_t tl_smem_bytes(int bm_words, int h_cap) {
          + 256 * 4                           // radix histogram
          + (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
-
-// k-th largest key (low bits cleared when passes < 4) among the N keys each
-// thread holds (key 0 = not an element). Histograms are private per warp
-// (`whist`, 256 words per warp) and summed per pass, so equal keys only
-// contend within a warp. Returns 0 when fewer than k elements exist. All
-// threads call; ends with __syncthreads().
-template <int N>
-__device__ uint32_t cta_kth_largest_warphist(const uint32_t (&keys)[N], int k, int passes,
-                                             uint32_t* whist, uint32_t* hist, int* sh) {
-  uint32_t prefix = 0u, mask = 0u;
-  int krem = k;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-#pragma unroll 1
-  for (int pass = 0; pass < passes; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < nw * 256; i += blockDim.x) whist[i] = 0u;
-    __syncthreads();
-    uint32_t* mine = whist + warp * 256;
-#pragma unroll
-    for (int j = 0; j < N; ++j)
-      if (keys[j] != 0u && (keys[j] & mask) == prefix) atomicAdd(&mine[(keys[j] >> shift) & 255u], 1u);
-    __syncthreads();
-    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
-      uint32_t s = 0u;
-      for (int w = 0; w < nw; ++w) s += whist[w * 256 + b];
-      hist[b] = s;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      int c[8];
-      int sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = (int)hist[255 - 8 * lane - j];
-        sum += c[j];
-      }
-      int incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int total = __shfl_sync(0xffffffffu, incl, 31);
-      if (lane == 0 && total < krem) {
-        sh[0] = -1;
-        sh[1] = 0;
-      }
-      const int excl = incl - sum;
-      if (total >= krem && excl < krem && krem <= incl) {
-        int run = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (run + c[j] >= krem) {
-            sh[0] = 255 - 8 * lane - j;
-            sh[1] = run;
-            break;
-          }
-          run += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    const int digit = sh[0];
-    if (digit < 0) {
-      __syncthreads();
-      return 0u;
-    }
-    krem -= sh[1];
-    prefix |= (uint32_t)digit << shift;
-    mask |= 0xFFu << shift;
-    __syncthreads();
-  }
-  return prefix;
-}
-
 
 constexpr int TL_NB = 1024;   // linear bins of the selection histograms (2 per thread)
 constexpr int TL_GCAP = 1024;  // candidates gathered by the final select (lower half of cv/cid)

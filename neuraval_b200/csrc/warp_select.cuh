@@ -316,44 +316,4 @@ __device__ __noinline__ void finish_weights_warp(const SampleArgs& a, int row, u
 }
 
 
-// One warp merges L <= 32 lists sorted by descending candidate key (value
-// desc, id asc) -- list l is keys(l, 0..n(l)) -- into out_v/out_i: the top K
-// plus every later entry equal in value to the K-th, in order, at most `cap`.
-// Returns the count, or -1 when the ties exceed `cap`. Each round takes the
-// largest list head (keys are unique: ids differ).
-template <typename KeyAt, typename LenOf>
-__device__ __noinline__ int warp_merge_topk(KeyAt key_at, LenOf len_of, int L, int K, float* out_v,
-                                            int* out_i, int cap) {
-  const int lane = threadIdx.x & 31;
-  int idx = 0;
-  const int n = lane < L ? len_of(lane) : 0;
-  uint64_t head = (lane < L && n > 0) ? key_at(lane, 0) : 0ull;
-  int m = 0;
-  uint32_t kval_key = 0u;
-  for (;;) {
-    uint64_t best = head;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t t = __shfl_xor_sync(0xffffffffu, best, o);
-      best = t > best ? t : best;
-    }
-    if (best == 0ull) break;
-    const uint32_t vkey = (uint32_t)(best >> 32);
-    if (m >= K && vkey != kval_key) break;
-    if (m >= cap) return -1;
-    if (lane == 0) {
-      out_v[m] = cand_val(best);
-      out_i[m] = cand_id(best);
-    }
-    ++m;
-    if (m == K) kval_key = vkey;
-    if (head == best) {
-      ++idx;
-      head = idx < n ? key_at(lane, idx) : 0ull;
-    }
-  }
-  __syncwarp();
-  return m;
-}
-
 }  // namespace nvs
