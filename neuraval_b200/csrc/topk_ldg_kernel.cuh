@@ -17,8 +17,10 @@
 //  - after the stream every warp publishes its 16 largest keys; ranks by
 //    binary search across those lists give the K-th value and the sorted
 //    candidates directly, weights are computed in parallel and one warp runs
-//    the sequential sums and the draw. Full lists, ties beyond 64 candidates
-//    and split rows fall back to histogram selects over all buffered values.
+//    the sequential sums and the draw (a split row's segments publish their
+//    sorted candidates and the last CTA ranks their union). Full lists and
+//    ties beyond 64 candidates fall back to histogram selects over all
+//    buffered values.
 // Penalties that can only lower a value (repetition >= 1, frequency and
 // presence >= 0) are applied to candidates only: raw*scale >= theta is a
 // superset test. Other penalties take the exact path for every float4 that
