@@ -45,9 +45,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="zipf_ranked", choices=["zipf_ranked", "vocab_sharded"],
+    ap.add_argument("--workload", default="zipf_ranked",
+                    choices=["zipf_ranked", "vocab_sharded", "softmax_rows"],
                     help="zipf_ranked: the headline (rows shard over GPUs); vocab_sharded: "
-                         "128 x 262144, vocabulary split over GPUs")
+                         "128 x 262144, vocabulary split over GPUs; softmax_rows: row softmax "
+                         "of the 256 x 128256 logits batch")
     return ap.parse_args()
 
 
@@ -184,6 +186,8 @@ def cpu_baseline(wl, seconds):
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
+    if args.workload == "softmax_rows":
+        return run_softmax_reference(args)
     wl = workload()
     from oracle import pyoracle
     pyoracle.build()
@@ -234,6 +238,8 @@ def main():
     try:
         if args.workload == "vocab_sharded":
             out = run_vocab_sharded(args, rank, world, dev)
+        elif args.workload == "softmax_rows":
+            out = run_softmax(args, rank, world, dev)
         else:
             out = run_rows(args, rank, world, dev)
         if rank == 0:
@@ -497,6 +503,126 @@ def run_vocab_sharded(args, rank, world, dev):
                "clocks": clocks.summary()}
     sampler.close()
     return out
+
+
+SOFTMAX_METRIC = "softmax rows/sec at B×V=256×128256 fp32"
+
+
+def _softmax_inputs(dev):
+    import torch
+    from neuraval_b200 import workloads
+    wl = workloads.zipf_ranked(H=1)
+    x = torch.from_numpy(wl["logits"]).to(dev)
+    bufs = [x] + [x.roll(i, dims=0).contiguous() for i in range(1, NBUF)]
+    return wl, bufs, torch.empty_like(x)
+
+
+def run_softmax(args, rank, world, dev):
+    """F-row: ncb_softmax_rows_device on the 256 x 128256 batch; each rank its own
+    copy (weak scaling), K launches in one CUDA graph."""
+    import ctypes
+    import torch
+    from neuraval_b200 import native, sharding
+    lib = native.load()
+    wl, bufs, out = _softmax_inputs(dev)
+    B, V = wl["logits"].shape
+
+    def step(i):
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        rc = lib.ncb_softmax_rows_device(ctypes.c_void_p(bufs[i % NBUF].data_ptr()),
+                                         ctypes.c_void_p(out.data_ptr()), B, V, st)
+        assert rc == 0, rc
+
+    cur = torch.cuda.current_stream(dev)
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(cur)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(args.steps):
+                step(i)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = ClockSampler(dev.index)
+    with clocks:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(cur)
+        graph.replay()
+        t1.record(cur)
+        torch.cuda.synchronize()
+    (total_ms,) = sharding.max_over_ranks([t0.elapsed_time(t1)], dev)
+    del graph
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peak()
+    per_launch_s = total_ms / args.steps / 1e3
+    alg = B * V * 8  # read the row once, write it once
+    return {"metric": SOFTMAX_METRIC, "value": world * B * args.steps / (total_ms / 1e3),
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
+            "config": {"workload": "softmax_rows_256x128256", "B": B, "V": V,
+                       "l2": f"inputs larger than L2: {NBUF} copies rotated across steps",
+                       "parallelism": f"each of {world} GPU(s) its own batch"},
+            "roofline": {"bound": "hbm", "achieved": alg / per_launch_s / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": alg / per_launch_s / 1e9 / peak,
+                         "peak_source": peak_kind, "traffic": None,
+                         "kernel": "softmax_rows_kernel",
+                         "algorithmic_bytes_per_launch": alg,
+                         "design_bytes_per_launch": B * V * 16},
+            "e2e": None, "gpu_launches": args.steps,
+            "timing": "CUDA events around one replay of a CUDA graph holding the K launches",
+            "clocks": clocks.summary()}
+
+
+def run_softmax_reference(args):
+    """The reference's own kernel (ncb_cuda_softmax_rows_device from its
+    navcuda.cu, compiled for sm_100a into oracle/_ref) on the same batch; it
+    launches on the legacy default stream, so it is timed eagerly."""
+    import ctypes
+    import torch
+    from oracle import refcuda
+    if not refcuda.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libnavcuda.so not built (needs the reference source)"}))
+        return 0
+    lib = refcuda.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    assert lib.ncb_cuda_init(0) == 1
+    wl, bufs, out = _softmax_inputs(dev)
+    B, V = wl["logits"].shape
+    step = lambda i: lib.ncb_cuda_softmax_rows_device(ctypes.c_void_p(bufs[i % NBUF].data_ptr()),
+                                                      ctypes.c_void_p(out.data_ptr()), B, V)
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    value = B * args.steps / (ms / 1e3)
+    print(json.dumps({"impl": "reference", "metric": SOFTMAX_METRIC, "value": value, "unit": UNIT,
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms / args.steps, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+                      "data": "synthetic", "config": {"workload": "softmax_rows_256x128256"},
+                      "cpu_baseline": {"value": value, "unit": UNIT, "cores": 0,
+                                       "kind": "reference",
+                                       "sample": "the reference's CUDA kernel, every launch on "
+                                                 "the GPU (its own implementation of this op)"},
+                      "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -211,6 +211,16 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* sampler, float* d_probs, 
                                            int vocab, float top_p, uint32_t* d_flags,
                                            void* stream);
 
+/* ---- row softmax ----------------------------------------------------------
+ * ncb_cuda_softmax_rows_device (Neuraval.Cuda.Native/src/navcuda.cu:673-700)
+ * with the arithmetic of its kernel (:616-671), output bits equal: row max,
+ * e = expf(x - max), 256 strided partial sums in element order and their
+ * tree, e / sum. d_out may equal d_in. rows <= 0 or cols <= 0 ->
+ * NCB_ERROR_INVALID_ARGUMENT (as the reference). Needs no handle;
+ * asynchronous on `stream`. */
+NCB_API int ncb_softmax_rows_device(const float* d_in, float* d_out, int rows, int cols,
+                                    void* stream);
+
 /* ---- status --------------------------------------------------------------- */
 /* ncb_cuda_last_status / ncb_cuda_status_message (navcuda.cu:982-1001). */
 NCB_API int ncb_sampler_last_status(void);

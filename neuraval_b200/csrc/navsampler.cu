@@ -56,6 +56,10 @@ int pow2_at_least(int x) {
 
 }  // namespace
 
+// The last status of every entry point, also for those compiled in other
+// translation units of the library (hidden symbol).
+int ncb_record_status(int st) { return set_status(st); }
+
 struct NcbSampler {
   int device = 0;
   int max_rows = 0, max_vocab = 0, max_history = 0;

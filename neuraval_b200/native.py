@@ -71,6 +71,7 @@ SIGNATURES = {
     "ncb_logits_temperature_device": (_I, [_P, _P, _I, _I, _F, _P]),
     "ncb_logits_filter_top_k_device": (_I, [_P, _P, _I, _I, _I, _P]),
     "ncb_logits_filter_top_p_device": (_I, [_P, _P, _I, _I, _F, _P, _P]),
+    "ncb_softmax_rows_device": (_I, [_P, _P, _I, _I, _P]),
     "ncb_sampler_last_status": (_I, []),
     "ncb_sampler_status_message": (ctypes.c_char_p, [_I]),
 }
