@@ -29,9 +29,10 @@ namespace nvs {
 
 constexpr int SMX_CHAINS = 256;   // the reference's NCB_REDUCE_THREADS
 constexpr int SMX_PREFETCH = 16;  // loads in flight per chain in the sums pass
-// Rows of one launch: their data (read three times) stays within half of L2,
-// so the second and third passes are L2 hits.
-constexpr size_t SMX_L2_BYTES = 48ull << 20;
+// Rows of one launch: their data (read three times) stays within this part of
+// the 126 MB L2, so the second and third passes are L2 hits.
+constexpr size_t SMX_L2_BYTES = 72ull << 20;
+constexpr int SMX_TILE = 8192;    // columns per shared-memory tile of the sums pass
 
 // One CTA per row. NT threads read in the order-free passes (maximum, outputs);
 // the first SMX_CHAINS of them run the partial sums.
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(NT) softmax_rows_kernel(const float* in, float
   __syncthreads();
 
   // ---- the 256 partial sums, each in element order, and their tree -------------
-  if (t < SMX_CHAINS) {
+  if constexpr (NT == SMX_CHAINS) {
     float s = 0.0f;
     int j = t;
     for (; j + (SMX_PREFETCH - 1) * SMX_CHAINS < cols; j += SMX_PREFETCH * SMX_CHAINS) {
@@ -88,6 +89,41 @@ __global__ void __launch_bounds__(NT) softmax_rows_kernel(const float* in, float
     }
     for (; j < cols; j += SMX_CHAINS) s += expf(__ldcg(x + j) - rmax);
     sh[t] = s;
+  } else {
+    // Tiles of SMX_TILE columns: every thread exponentiates NT-strided columns
+    // of the tile into shared memory (the next tile's loads already in flight),
+    // then chain t adds columns t, t+256, ... of the tile in order. Columns past
+    // the row add +0, which leaves a sum unchanged.
+    constexpr int PER = SMX_TILE / NT;
+    __shared__ float tile[SMX_TILE];
+    float s = 0.0f;
+    float v[PER], w[PER];  // this tile's and the next tile's columns, loads in flight
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int j = t + u * NT;
+      v[u] = j < cols ? __ldcg(x + j) : 0.0f;
+      w[u] = j + SMX_TILE < cols ? __ldcg(x + j + SMX_TILE) : 0.0f;
+    }
+    for (int base = 0; base < cols; base += SMX_TILE) {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int j = base + t + u * NT;
+        tile[t + u * NT] = j < cols ? expf(v[u] - rmax) : 0.0f;
+        v[u] = w[u];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int j = base + 2 * SMX_TILE + t + u * NT;
+        w[u] = j < cols ? __ldcg(x + j) : 0.0f;
+      }
+      if (t < SMX_CHAINS) {
+#pragma unroll 8
+        for (int k = 0; k < SMX_TILE / SMX_CHAINS; ++k) s += tile[k * SMX_CHAINS + t];
+      }
+      __syncthreads();
+    }
+    if (t < SMX_CHAINS) sh[t] = s;
   }
   __syncthreads();
   for (int stride = SMX_CHAINS / 2; stride > 0; stride >>= 1) {
@@ -125,8 +161,10 @@ extern "C" NCB_API int ncb_softmax_rows_device(const float* d_in, float* d_out, 
   // rows go in launches whose data fits the L2 budget (passes 2 and 3 re-read it)
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t row_bytes = (size_t)cols * 4;
-  int chunk = (int)(nvs::SMX_L2_BYTES / row_bytes);
-  if (chunk < 1) chunk = 1;
+  int fit = (int)(nvs::SMX_L2_BYTES / row_bytes);
+  if (fit < 1) fit = 1;
+  const int groups = (rows + fit - 1) / fit;
+  const int chunk = (rows + groups - 1) / groups;  // equal groups keep every launch full
   for (int r0 = 0; r0 < rows; r0 += chunk) {
     const int n = rows - r0 < chunk ? rows - r0 : chunk;
     const float* i0 = d_in + (size_t)r0 * cols;
