@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="vocab_sharded: records exchanged by an NCCL all-gather, or through "
+                         "peer memory by the shard kernel itself")
     ap.add_argument("--workload", default="zipf_ranked",
                     choices=["zipf_ranked", "vocab_sharded", "softmax_rows"],
                     help="zipf_ranked: the headline (rows shard over GPUs); vocab_sharded: "
@@ -405,6 +408,7 @@ def run_vocab_sharded(args, rank, world, dev):
     words = sampler.shard_record_bytes // 4
     local = torch.zeros((B, words), dtype=torch.int32, device=dev)
     gathered = torch.zeros((world, B, words), dtype=torch.int32, device=dev)
+    peer = sharding.PeerVocabShardedSampler(sampler, V) if args.exchange == "peer" else None
 
     def candidates(i):
         sampler.shard_candidates_device(bufs[i % nbuf], V, lo, hist, offs, params, local,
@@ -417,13 +421,21 @@ def run_vocab_sharded(args, rank, world, dev):
             gathered[0].copy_(local)
 
     def merge(i):
-        sampler.shard_merge_device(gathered, world, B, V, u, params, tokens, flags,
-                                   torch.cuda.current_stream(dev))
+        if peer is not None:
+            sampler.shard_merge_peer_device(B, V, u, params, tokens, flags,
+                                            torch.cuda.current_stream(dev))
+        else:
+            sampler.shard_merge_device(gathered, world, B, V, u, params, tokens, flags,
+                                       torch.cuda.current_stream(dev))
 
     def full(i):
-        candidates(i)
-        exchange(i)
-        merge(i)
+        if peer is not None:
+            peer.sample(bufs[i % nbuf], hist, offs, u, params, tokens, flags,
+                        torch.cuda.current_stream(dev))
+        else:
+            candidates(i)
+            exchange(i)
+            merge(i)
 
     cur = torch.cuda.current_stream(dev)
     for i in range(max(3, args.warmup)):
@@ -455,7 +467,12 @@ def run_vocab_sharded(args, rank, world, dev):
 
     clocks = ClockSampler(dev.index)
     total_ms = timed(full, clocks)
-    parts = [timed(candidates), timed(exchange), timed(merge)]
+    if peer is not None:
+        # a merge alone re-reads the last call's records (its flags are already set)
+        parts = [timed(candidates), 0.0, timed(merge)]
+        parts[1] = max(0.0, total_ms - parts[0] - parts[2])
+    else:
+        parts = [timed(candidates), timed(exchange), timed(merge)]
     total_ms, *parts = sharding.max_over_ranks([total_ms] + parts, dev)
     # the sampled tokens equal the single-GPU sampler's on the whole rows
     ok = True
@@ -482,13 +499,16 @@ def run_vocab_sharded(args, rank, world, dev):
                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
                "config": config_of(wl, {"parallelism": f"vocabulary sharded over {world} GPU(s);"
-                                                       " records all-gathered (NCCL)",
+                                                       f" {args.exchange} record exchange",
                                         "l2": f"{nbuf} rotated copies of each shard",
                                         "shard_columns": width,
                                         "record_bytes_per_rank": B * sampler.shard_record_bytes}),
                "parts_us_per_step": {"candidates": parts[0] / args.steps * 1e3,
-                                     "all_gather": parts[1] / args.steps * 1e3,
+                                     "exchange": parts[1] / args.steps * 1e3,
                                      "merge": parts[2] / args.steps * 1e3},
+               "exchange": ("records stored into every GPU's exchange area over NVLink by the "
+                            "library (epoch flags and acks)" if peer is not None else
+                            "NCCL all-gather of the records"),
                "tokens_match_single_gpu": ok,
                "roofline": {"bound": "hbm", "achieved": per_gpu_bytes / per_step_s / 1e9,
                             "peak": peak, "unit": "GB/s",
@@ -497,7 +517,7 @@ def run_vocab_sharded(args, rank, world, dev):
                             "kernel": "shard candidate kernel + all-gather + merge, per step",
                             "algorithmic_bytes_per_launch": per_gpu_bytes},
                "e2e": None,
-               "gpu_launches": 2 * args.steps,  # candidates + merge (NCCL's kernel not counted)
+               "gpu_launches": (3 if peer is not None else 2) * args.steps,
                "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
                          "(all-gather included); max over ranks",
                "clocks": clocks.summary()}

@@ -211,6 +211,33 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* sampler, float* d_probs, 
                                            int vocab, float top_p, uint32_t* d_flags,
                                            void* stream);
 
+/* The same exchange done by the library through peer memory, without a
+ * collective (no reference counterpart). Each GPU's handle owns one exchange
+ * area: ncb_vocab_shard_peer_setup allocates it and writes its CUDA IPC handle
+ * (ncb_peer_handle_bytes() bytes); the caller gives every handle all handles
+ * in shard order (ncb_vocab_shard_peer_connect; handles exported by the same
+ * process resolve without IPC). Per call, on every GPU in the same order:
+ * ncb_vocab_shard_push_peer_device (shard kernel, then its records are stored
+ * into every GPU's area over NVLink and an epoch flag is released there) and
+ * ncb_vocab_shard_merge_peer_device (waits for every shard's flag, merges,
+ * releases an ack that lets the peers overwrite its area on the next call).
+ * Every wait is bounded (about 2 s); a merge that gives up returns token -1
+ * with NCB_FLAG_PEER_TIMEOUT. rows <= the handle's max_rows; all GPUs pass the
+ * same rows, vocab and params. */
+#define NCB_FLAG_PEER_TIMEOUT 0x80u
+NCB_API int ncb_peer_handle_bytes(void);
+NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* sampler, int shards, int me, void* handle_out);
+NCB_API int ncb_vocab_shard_peer_connect(NcbSampler* sampler, const void* handles);
+NCB_API int ncb_vocab_shard_push_peer_device(NcbSampler* sampler, const float* d_logits, int rows,
+                                             int vocab, int col_begin, int col_end, int ld,
+                                             const int32_t* d_hist,
+                                             const int32_t* d_hist_offsets,
+                                             const NcbSamplerParams* params, void* stream);
+NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* sampler, int rows, int vocab,
+                                              const float* d_uniforms,
+                                              const NcbSamplerParams* params, int32_t* d_tokens,
+                                              uint32_t* d_flags, void* stream);
+
 /* ---- row softmax ----------------------------------------------------------
  * ncb_cuda_softmax_rows_device (Neuraval.Cuda.Native/src/navcuda.cu:673-700)
  * with the arithmetic of its kernel (:616-671), output bits equal: row max,

@@ -12,7 +12,9 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <array>
 #include <mutex>
+#include <vector>
 
 #include "fullvocab_kernels.cuh"
 #include "logits_ops.cuh"
@@ -82,7 +84,22 @@ struct NcbSampler {
   float* h_probs_dev = nullptr;
   size_t h_hist_cap = 0;
   cudaStream_t host_stream = nullptr;
+  // vocabulary shards exchanged through peer memory
+  char* px_area = nullptr;  // this GPU's exchange area (records, flags, acks)
+  int px_shards = 0, px_me = -1;
+  bool px_connected = false;
+  nvs::PeerLayout px_layout{};
+  char* px_base[nvs::PX_MAX] = {};  // every shard's area as mapped here
+  bool px_imported[nvs::PX_MAX] = {};
+  bool px_pushed = false;
 };
+
+namespace {
+// Exchange areas exported by this process: a handle of our own resolves to
+// the pointer directly (CUDA IPC does not open a process's own handles).
+std::mutex g_px_mu;
+std::vector<std::pair<std::array<char, sizeof(cudaIpcMemHandle_t)>, char*>> g_px_local;
+}  // namespace
 
 static bool params_ok(const NcbSamplerParams* p) {
   if (!p) return false;
@@ -226,6 +243,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   const size_t o_gi = carve(mc * sizeof(int32_t));
   const size_t o_er = carve(sizeof(uint32_t));
   const size_t o_fx = carve((size_t)max_rows * sizeof(uint32_t));
+  const size_t o_px = carve(4 * sizeof(uint32_t));
   const nvs::FvLayout fl = nvs::fv_layout(max_rows, max_vocab);
   const size_t o_fv = carve(fl.total_bytes);
   if (cudaMalloc(&h->scratch, off) != cudaSuccess) {
@@ -242,6 +260,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->s.gi = reinterpret_cast<int32_t*>(b + o_gi);
   h->s.error_word = reinterpret_cast<uint32_t*>(b + o_er);
   h->s.fixup = reinterpret_cast<uint32_t*>(b + o_fx);
+  h->s.px_ticket = reinterpret_cast<uint32_t*>(b + o_px);
   h->fv = nvs::fv_carve(b + o_fv, fl);
   // tickets/rowstate/error word must start at zero; the kernels restore zero
   if (!raise_smem_limits(h->max_smem_optin) || cudaMemset(h->scratch, 0, off) != cudaSuccess ||
@@ -259,6 +278,17 @@ NCB_API int ncb_sampler_destroy(NcbSampler* h) {
   {
     DeviceGuard g(h->device);
     cudaDeviceSynchronize();
+    if (h->px_area) {
+      for (int s = 0; s < nvs::PX_MAX; ++s)
+        if (h->px_imported[s]) cudaIpcCloseMemHandle(h->px_base[s]);
+      std::lock_guard<std::mutex> lk(g_px_mu);
+      for (size_t i = 0; i < g_px_local.size(); ++i)
+        if (g_px_local[i].second == h->px_area) {
+          g_px_local.erase(g_px_local.begin() + i);
+          break;
+        }
+      cudaFree(h->px_area);
+    }
     cudaFree(h->scratch);
     cudaFree(h->h_logits_dev);
     cudaFree(h->h_hist_dev);
@@ -694,6 +724,92 @@ extern "C" NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int
 }
 
 // ---- vocabulary shards ------------------------------------------------------
+
+static int check_shard_args(NcbSampler* h, const float* d_logits, int rows, int vocab,
+                            int col_begin, int col_end, int ld, const int32_t* d_hoff,
+                            const NcbSamplerParams* prm) {
+  if (!h) return NCB_ERROR_NOT_INITIALIZED;
+  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0 || col_begin < 0 ||
+      col_end <= col_begin || col_end > vocab || ld < col_end - col_begin)
+    return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows == 0) return NCB_OK;
+  if (!d_logits || !d_hoff || (reinterpret_cast<uintptr_t>(d_logits) & 3u) != 0u)
+    return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows > h->max_rows || col_end - col_begin > h->max_vocab) return NCB_ERROR_CAPACITY;
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  if (!prm->greedy && K > nvs::TL_KMAX) return NCB_ERROR_CAPACITY;
+  return NCB_OK;
+}
+
+// The shard kernel for one column range; caller holds h->mu and the device.
+static int launch_shard_candidates(NcbSampler* h, const float* d_logits, int rows, int vocab,
+                                   int col_begin, int col_end, int ld, const int32_t* d_hist,
+                                   const int32_t* d_hoff, const NcbSamplerParams* prm,
+                                   uint32_t* records, cudaStream_t stream,
+                                   const nvs::PxArgs* px = nullptr) {
+  const int width = col_end - col_begin;
+  nvs::SampleArgs a{};
+  if (px) a.px = *px;
+  a.logits = d_logits;
+  a.V = vocab;
+  a.hist = d_hist;
+  a.hoff = d_hoff;
+  a.p = to_params(prm);
+  a.s = h->s;
+  a.ld = ld;
+  a.col_lo = col_begin;
+  a.col_hi = col_end;
+  a.shard_out = records;
+  const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
+  a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
+  int S = choose_splits(rows, width, h->num_sms, h->forced_splits);
+  a.seg_len = round_up((width + S - 1) / S, 4);
+  S = (width + a.seg_len - 1) / a.seg_len;
+  if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
+  a.bm_words = (a.seg_len + 31) / 32 + 1;
+  dim3 grid(S, rows);
+  if (prm->greedy) {
+    const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+    if (counts) nvs::greedy_kernel<true, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+    else nvs::greedy_kernel<false, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
+  } else {
+    const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+    if (counts) nvs::topk_ldg_kernel<true, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    else nvs::topk_ldg_kernel<false, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+  }
+  return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
+}
+
+// The merge kernel; with wait_flags it first waits for the peers' records of
+// `epoch` and finally releases acks[] (peer-memory exchange).
+static int launch_merge(NcbSampler* h, const uint32_t* recs, int shards, int rows, int vocab,
+                        const float* d_u, const NcbSamplerParams* prm, int32_t* d_tok,
+                        uint32_t* d_flags, const uint32_t* wait_flags,
+                        uint32_t* const* acks, cudaStream_t stream) {
+  nvs::MergeArgs m{};
+  m.recs = recs;
+  m.shards = shards;
+  m.rows = rows;
+  m.a.V = vocab;
+  m.a.uniforms = d_u;
+  m.a.p = to_params(prm);
+  m.a.tokens = d_tok;
+  m.a.flags = d_flags;
+  m.a.s = h->s;
+  m.wait_flags = wait_flags;
+  m.epoch = h->s.px_ticket + 3;
+  if (acks) {
+    for (int s = 0; s < shards; ++s) m.ack[s] = acks[s];
+    m.ticket = h->s.px_ticket + 2;
+  }
+  const size_t smem = nvs::vm_smem_bytes();
+  if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+  nvs::vocab_merge_kernel<<<rows, nvs::VM_THREADS, smem, stream>>>(m);
+  return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
+}
+
 //
 // A batch whose vocabulary is split in contiguous column ranges over several
 // GPUs: each GPU reduces its range of every row to a fixed-size record
@@ -712,55 +828,16 @@ NCB_API int ncb_vocab_shard_candidates_device(NcbSampler* h, const float* d_logi
                                               const int32_t* d_hist_offsets,
                                               const NcbSamplerParams* prm, void* d_records,
                                               void* stream_) {
-  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
-  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0 || col_begin < 0 ||
-      col_end <= col_begin || col_end > vocab || ld < col_end - col_begin)
+  int st = check_shard_args(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist_offsets, prm);
+  if (st != NCB_OK || rows == 0) return set_status(st);
+  if (!d_records || (reinterpret_cast<uintptr_t>(d_records) & 3u) != 0u)
     return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  if (rows == 0) return set_status(NCB_OK);
-  if (!d_logits || !d_hist_offsets || !d_records) return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  if ((reinterpret_cast<uintptr_t>(d_logits) & 3u) != 0u ||
-      (reinterpret_cast<uintptr_t>(d_records) & 3u) != 0u)
-    return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  const int width = col_end - col_begin;
-  if (rows > h->max_rows || width > h->max_vocab) return set_status(NCB_ERROR_CAPACITY);
-  const int K = prm->top_k < vocab ? prm->top_k : vocab;
-  if (!prm->greedy && K > nvs::TL_KMAX) return set_status(NCB_ERROR_CAPACITY);
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-
-  nvs::SampleArgs a{};
-  a.logits = d_logits;
-  a.V = vocab;
-  a.hist = d_hist;
-  a.hoff = d_hist_offsets;
-  a.p = to_params(prm);
-  a.s = h->s;
-  a.ld = ld;
-  a.col_lo = col_begin;
-  a.col_hi = col_end;
-  a.shard_out = static_cast<uint32_t*>(d_records);
-  const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
-  a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
-  int S = choose_splits(rows, width, h->num_sms, h->forced_splits);
-  a.seg_len = round_up((width + S - 1) / S, 4);
-  S = (width + a.seg_len - 1) / a.seg_len;
-  if ((size_t)rows * S > (size_t)h->max_ctas) return set_status(NCB_ERROR_CAPACITY);
-  a.bm_words = (a.seg_len + 31) / 32 + 1;
-  dim3 grid(S, rows);
-  if (prm->greedy) {
-    const size_t smem = (size_t)a.bm_words * 4 + (size_t)a.h_cap * 4;
-    if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
-    if (counts) nvs::greedy_kernel<true, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
-    else nvs::greedy_kernel<false, true><<<grid, nvs::GR_THREADS, smem, stream>>>(a);
-  } else {
-    const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
-    if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
-    if (counts) nvs::topk_ldg_kernel<true, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
-    else nvs::topk_ldg_kernel<false, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
-  }
-  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+  return set_status(launch_shard_candidates(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist,
+                                            d_hist_offsets, prm, static_cast<uint32_t*>(d_records),
+                                            static_cast<cudaStream_t>(stream_)));
 }
 
 NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, int shards,
@@ -780,20 +857,142 @@ NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, i
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  nvs::MergeArgs m{};
-  m.recs = static_cast<const uint32_t*>(d_records);
-  m.shards = shards;
-  m.rows = rows;
-  m.a.V = vocab;
-  m.a.uniforms = d_uniforms;
-  m.a.p = to_params(prm);
-  m.a.tokens = d_tokens;
-  m.a.flags = d_flags;
-  m.a.s = h->s;
-  const size_t smem = nvs::vm_smem_bytes();
-  if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
-  nvs::vocab_merge_kernel<<<rows, nvs::VM_THREADS, smem, static_cast<cudaStream_t>(stream_)>>>(m);
-  return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+  return set_status(launch_merge(h, static_cast<const uint32_t*>(d_records), shards, rows, vocab,
+                                 d_uniforms, prm, d_tokens, d_flags, nullptr, nullptr,
+                                 static_cast<cudaStream_t>(stream_)));
+}
+
+}  // extern "C"
+
+// ---- vocabulary shards through peer memory ------------------------------------
+//
+// The exchange of ncb_vocab_shard_* done by the library itself: the shard
+// kernel stores every finished record straight into the other GPUs' exchange
+// areas over NVLink (CUDA IPC mappings) and releases an epoch flag; the merge
+// waits for the flags and acks back. No collective, no extra kernel.
+
+extern "C" {
+
+NCB_API int ncb_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* h, int shards, int me, void* handle_out) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (shards < 1 || shards > nvs::PX_MAX || me < 0 || me >= shards || !handle_out || h->px_area)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  const nvs::PeerLayout l = nvs::peer_layout(shards, h->max_rows);
+  void* area = nullptr;
+  if (cudaMalloc(&area, l.bytes) != cudaSuccess) return set_status(NCB_ERROR_ALLOC_FAILED);
+  cudaIpcMemHandle_t hd;
+  if (cudaMemset(area, 0, l.bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&hd, area) != cudaSuccess) {
+    cudaFree(area);
+    return set_status(NCB_ERROR_INIT_FAILED);
+  }
+  std::memcpy(handle_out, &hd, sizeof(hd));
+  {
+    std::lock_guard<std::mutex> lk2(g_px_mu);
+    std::array<char, sizeof(cudaIpcMemHandle_t)> key;
+    std::memcpy(key.data(), &hd, sizeof(hd));
+    g_px_local.emplace_back(key, static_cast<char*>(area));
+  }
+  h->px_area = static_cast<char*>(area);
+  h->px_shards = shards;
+  h->px_me = me;
+  h->px_layout = l;
+  h->px_base[me] = h->px_area;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_vocab_shard_peer_connect(NcbSampler* h, const void* handles) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!h->px_area || h->px_connected || !handles) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  const char* hb = static_cast<const char*>(handles);
+  for (int s = 0; s < h->px_shards; ++s) {
+    if (s == h->px_me) continue;
+    std::array<char, sizeof(cudaIpcMemHandle_t)> key;
+    std::memcpy(key.data(), hb + (size_t)s * sizeof(cudaIpcMemHandle_t), key.size());
+    char* local = nullptr;
+    {
+      std::lock_guard<std::mutex> lk2(g_px_mu);
+      for (const auto& e : g_px_local)
+        if (e.first == key) local = e.second;
+    }
+    if (local) {
+      h->px_base[s] = local;
+      continue;
+    }
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, key.data(), sizeof(hd));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return set_status(NCB_ERROR_INIT_FAILED);
+    h->px_base[s] = static_cast<char*>(p);
+    h->px_imported[s] = true;
+  }
+  h->px_connected = true;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_vocab_shard_push_peer_device(NcbSampler* h, const float* d_logits, int rows,
+                                             int vocab, int col_begin, int col_end, int ld,
+                                             const int32_t* d_hist,
+                                             const int32_t* d_hist_offsets,
+                                             const NcbSamplerParams* prm, void* stream_) {
+  int st = check_shard_args(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist_offsets, prm);
+  if (st != NCB_OK || rows == 0) return set_status(st);
+  if (!h->px_connected) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  h->px_pushed = true;
+  const size_t slot_bytes = (size_t)rows * nvs::VS_REC_WORDS * 4;
+  uint32_t* own = reinterpret_cast<uint32_t*>(h->px_area + (size_t)h->px_me * slot_bytes);
+  nvs::PxArgs px{};
+  for (int s = 0; s < h->px_shards; ++s) {
+    px.dst[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + (size_t)h->px_me * slot_bytes);
+    px.flag[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + h->px_layout.flags_off) + h->px_me;
+  }
+  px.acks = reinterpret_cast<const uint32_t*>(h->px_area + h->px_layout.acks_off);
+  px.ticket = h->s.px_ticket;
+  px.epoch = h->s.px_ticket + 3;
+  px.shards = h->px_shards;
+  px.me = h->px_me;
+  // the shard kernel stores each finished record into every peer's area itself
+  st = launch_shard_candidates(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist,
+                               d_hist_offsets, prm, own, stream, &px);
+  return set_status(st);
+}
+
+NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* h, int rows, int vocab,
+                                              const float* d_uniforms,
+                                              const NcbSamplerParams* prm, int32_t* d_tokens,
+                                              uint32_t* d_flags, void* stream_) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!prm || !params_ok(prm) || rows < 0 || vocab <= 0) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  if (!h->px_connected || !h->px_pushed) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (rows == 0) return set_status(NCB_OK);
+  if (rows > h->max_rows || !d_tokens || (!prm->greedy && !d_uniforms))
+    return set_status(rows > h->max_rows ? NCB_ERROR_CAPACITY : NCB_ERROR_INVALID_ARGUMENT);
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  if (!prm->greedy && K > nvs::TL_KMAX) return set_status(NCB_ERROR_CAPACITY);
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  uint32_t* acks[nvs::PX_MAX] = {};
+  for (int s = 0; s < h->px_shards; ++s)
+    if (s != h->px_me)
+      acks[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + h->px_layout.acks_off) + h->px_me;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(h->px_area + h->px_layout.flags_off);
+  return set_status(launch_merge(h, reinterpret_cast<const uint32_t*>(h->px_area), h->px_shards,
+                                 rows, vocab, d_uniforms, prm, d_tokens, d_flags, flags, acks,
+                                 static_cast<cudaStream_t>(stream_)));
 }
 
 }  // extern "C"

@@ -19,6 +19,7 @@
 
 #include "sampler_device.cuh"
 #include "shard_record.cuh"
+#include "peer_exchange.cuh"
 
 namespace nvs {
 
@@ -39,6 +40,8 @@ struct Scratch {
   int32_t* gi;          // [max_ctas]
   uint32_t* error_word; // [1] sticky error bits (timeouts)
   uint32_t* fixup;      // [max_rows]  1: row must be redone on the full-vocabulary path
+  uint32_t* px_ticket;  // [4] peer exchange: push CTAs, failed push waits, merge CTAs (zero
+                        // between launches), epoch of the last call
 };
 
 struct SampleArgs {
@@ -62,6 +65,7 @@ struct SampleArgs {
   int col_lo;
   int col_hi;
   uint32_t* shard_out;
+  PxArgs px;            // peers of a shard kernel (px.shards == 0: none)
 };
 
 // Shared penalty state for the CTA's column range [c0,c1). Returns false when
@@ -138,8 +142,24 @@ __device__ __forceinline__ Best warp_best(Best b) {
   return b;
 }
 
+template <bool kCounts, bool kShard>
+__device__ __forceinline__ void greedy_body(const SampleArgs& a, int* owner);
+
 template <bool kCounts, bool kShard = false>
 __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constant__ SampleArgs a) {
+  __shared__ int s_owner;
+  greedy_body<kCounts, kShard>(a, &s_owner);
+  if constexpr (kShard) {
+    if (a.px.shards > 0) {
+      __syncthreads();
+      shard_px_epilogue(a.px, a.shard_out + (size_t)blockIdx.y * VS_REC_WORDS, blockIdx.y,
+                        s_owner != 0);
+    }
+  }
+}
+
+template <bool kCounts, bool kShard>
+__device__ __forceinline__ void greedy_body(const SampleArgs& a, int* owner) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem);
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
@@ -154,6 +174,7 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
   const int c0 = lo + split * a.seg_len;
   const int c1 = min(hi, c0 + a.seg_len);
   const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * V;
+  if (threadIdx.x == 0) *owner = S == 1;  // the CTA that writes the row's result
 
   Penalty P;
   const bool ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
@@ -203,6 +224,7 @@ __global__ void __launch_bounds__(GR_THREADS) greedy_kernel(const __grid_constan
     __threadfence();
     const uint32_t t = atomicAdd(&a.s.tickets[row], 1u);
     s_last = (t == (uint32_t)(S - 1));
+    *owner = s_last;
   }
   __syncthreads();
   if (!s_last) return;

@@ -204,9 +204,25 @@ __device__ float cta_select_linear(const float (&v)[N], const bool (&valid)[N], 
   return kval(key);
 }
 
+template <bool kCounts, bool kShard>
+__device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner);
+
 template <bool kCounts, bool kShard = false>
 __global__ void __launch_bounds__(TL_THREADS, 2)
     topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
+  __shared__ int s_owner;
+  topk_ldg_body<kCounts, kShard>(a, &s_owner);
+  if constexpr (kShard) {
+    if (a.px.shards > 0) {
+      __syncthreads();
+      shard_px_epilogue(a.px, a.shard_out + (size_t)blockIdx.y * VS_REC_WORDS, blockIdx.y,
+                        s_owner != 0);
+    }
+  }
+}
+
+template <bool kCounts, bool kShard>
+__device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* wvall = reinterpret_cast<float*>(smem);                           // [W][WCAP]
   int* wiall = reinterpret_cast<int*>(wvall + TL_WARPS * TW_WCAP);         // [W][WCAP]
@@ -238,6 +254,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   const int c1 = min(hi, c0 + a.seg_len);
   // shard rows are addressed by global column: lrow[c] for c in [lo, hi)
   const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * V;
+  if (tid == 0) *owner = S == 1;  // the CTA that writes the row's result
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
 
   // 16-byte aligned body [a0,a1) as float4; <=3 head and <=3 tail scalars
@@ -773,6 +790,7 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
     __threadfence();
     const uint32_t t = atomicAdd(&a.s.tickets[row], 1u);
     s_last = (t == (uint32_t)(S - 1));
+    *owner = s_last;
   }
   __syncthreads();
   if (!s_last) return;

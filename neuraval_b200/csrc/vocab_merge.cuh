@@ -12,6 +12,7 @@
 #include "topk_kernels.cuh"
 #include "warp_select.cuh"
 #include "rank_select.cuh"
+#include "peer_exchange.cuh"
 
 namespace nvs {
 
@@ -26,9 +27,49 @@ struct MergeArgs {
   int shards;
   int rows;
   SampleArgs a;          // V = full vocabulary, p, uniforms, tokens, flags (probs unused)
+  // peer-memory exchange only (null otherwise): wait until flags[0..shards)
+  // reach epoch, then release acks to every peer from the last CTA
+  const uint32_t* wait_flags;
+  const uint32_t* epoch;  // the push kernel's epoch word
+  uint32_t* ack[PX_MAX];
+  uint32_t* ticket;      // local, zero between launches
 };
 
+__device__ void merge_row(const MergeArgs& g);
+
 __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_constant__ MergeArgs g) {
+  __shared__ int s_ok, s_last;
+  __shared__ uint32_t s_epoch;
+  const int tid = threadIdx.x;
+  if (g.wait_flags) {
+    if (tid == 0) {
+      s_epoch = __ldcg(g.epoch);
+      s_ok = wait_words_bounded(g.wait_flags, g.shards, s_epoch) ? 1 : 0;
+    }
+    __syncthreads();
+    if (s_ok) {
+      merge_row(g);
+    } else if (tid == 0) {
+      g.a.tokens[blockIdx.x] = -1;
+      if (g.a.flags) g.a.flags[blockIdx.x] = FLAG_PEER_TIMEOUT;
+    }
+  } else {
+    merge_row(g);
+  }
+  if (g.ticket) {
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(g.ticket, 1u) == gridDim.x - 1u;
+    __syncthreads();
+    if (s_last && tid == 0) {
+      __threadfence_system();
+      for (int s = 0; s < g.shards; ++s)
+        if (g.ack[s]) st_release_sys(g.ack[s], s_epoch);
+      *g.ticket = 0u;
+    }
+  }
+}
+
+__device__ void merge_row(const MergeArgs& g) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* cv = reinterpret_cast<float*>(smem);                            // [CAPB]
   int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                       // [CAPB]

@@ -29,6 +29,7 @@ FLAG_NONFINITE = 0x8
 FLAG_EXP_SLOW = 0x10
 FLAG_BAD_HISTORY = 0x20
 FLAG_TIES_OVERFLOW = 0x40
+FLAG_PEER_TIMEOUT = 0x80
 # rows whose token may legitimately differ from the reference's
 PARITY_EXEMPT = FLAG_DRAW_BOUNDARY | FLAG_CUTOFF_BOUNDARY | FLAG_TIE_AT_DRAW
 
@@ -71,6 +72,13 @@ SIGNATURES = {
     "ncb_logits_temperature_device": (_I, [_P, _P, _I, _I, _F, _P]),
     "ncb_logits_filter_top_k_device": (_I, [_P, _P, _I, _I, _I, _P]),
     "ncb_logits_filter_top_p_device": (_I, [_P, _P, _I, _I, _F, _P, _P]),
+    "ncb_peer_handle_bytes": (_I, []),
+    "ncb_vocab_shard_peer_setup": (_I, [_P, _I, _I, _P]),
+    "ncb_vocab_shard_peer_connect": (_I, [_P, _P]),
+    "ncb_vocab_shard_push_peer_device": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P,
+                                              ctypes.POINTER(NcbSamplerParams), _P]),
+    "ncb_vocab_shard_merge_peer_device": (_I, [_P, _I, _I, _P, ctypes.POINTER(NcbSamplerParams),
+                                               _P, _P, _P]),
     "ncb_softmax_rows_device": (_I, [_P, _P, _I, _I, _P]),
     "ncb_sampler_last_status": (_I, []),
     "ncb_sampler_status_message": (ctypes.c_char_p, [_I]),

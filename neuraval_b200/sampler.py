@@ -115,6 +115,35 @@ class CudaTokenSampler:
             ctypes.byref(params), _ptr(tokens), _ptr(flags), _stream_ptr(stream)),
             "ncb_vocab_shard_merge_device")
 
+    # vocabulary shards exchanged through peer memory
+    def peer_setup(self, shards: int, me: int) -> bytes:
+        """Allocates this GPU's exchange area; returns its IPC handle."""
+        n = int(self._lib.ncb_peer_handle_bytes())
+        buf = ctypes.create_string_buffer(n)
+        check(self._lib.ncb_vocab_shard_peer_setup(self._h, int(shards), int(me), buf),
+              "ncb_vocab_shard_peer_setup")
+        return buf.raw
+
+    def peer_connect(self, handles: bytes) -> None:
+        """`handles`: every shard's handle, concatenated in shard order."""
+        buf = ctypes.create_string_buffer(handles, len(handles))
+        check(self._lib.ncb_vocab_shard_peer_connect(self._h, buf), "ncb_vocab_shard_peer_connect")
+
+    def shard_push_peer_device(self, logits_shard, vocab: int, col_begin: int, hist_ids,
+                               hist_offsets, params: NcbSamplerParams, stream=None) -> None:
+        rows, width = int(logits_shard.shape[0]), int(logits_shard.shape[1])
+        ld = int(logits_shard.stride(0)) if rows > 1 else width
+        check(self._lib.ncb_vocab_shard_push_peer_device(
+            self._h, _ptr(logits_shard), rows, int(vocab), int(col_begin), int(col_begin) + width,
+            ld, _ptr(hist_ids), _ptr(hist_offsets), ctypes.byref(params), _stream_ptr(stream)),
+            "ncb_vocab_shard_push_peer_device")
+
+    def shard_merge_peer_device(self, rows: int, vocab: int, uniforms, params: NcbSamplerParams,
+                                tokens, flags=None, stream=None) -> None:
+        check(self._lib.ncb_vocab_shard_merge_peer_device(
+            self._h, int(rows), int(vocab), _ptr(uniforms), ctypes.byref(params), _ptr(tokens),
+            _ptr(flags), _stream_ptr(stream)), "ncb_vocab_shard_merge_peer_device")
+
     # ---- LogitsProcessor (in place, device tensors) ----------------------
     def repetition_penalty_(self, logits, hist_ids, hist_offsets, penalty, stream=None):
         check(self._lib.ncb_logits_repetition_penalty_device(

@@ -44,8 +44,10 @@ def gather_records(local, group=None):
     rank order (= column order for vocabulary shards)."""
     import torch
     import torch.distributed as dist
-    world = dist.get_world_size(group)
     local = local.contiguous()
+    if not dist.is_initialized():
+        return local.unsqueeze(0)
+    world = dist.get_world_size(group)
     out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(out, local, group=group)
@@ -77,8 +79,8 @@ class VocabShardedSampler:
         self.sampler = sampler
         self.vocab = int(vocab)
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.col_begin, self.col_end = vocab_range(self.vocab, self.world, self.rank)
         self.rec_words = sampler.shard_record_bytes // 4
         self._local = None
@@ -116,3 +118,34 @@ class VocabShardedSampler:
             self.sampler.shard_merge_device(gathered, self.world, rows, self.vocab, uniforms,
                                             params, tokens, flags, cur)
 
+
+
+class PeerVocabShardedSampler(VocabShardedSampler):
+    """VocabShardedSampler whose exchange is done by the library through peer
+    memory (records stored into every GPU's exchange area over NVLink, epoch
+    flags and acks) instead of an NCCL all-gather. The process group is used
+    once, to exchange the areas' IPC handles."""
+
+    def __init__(self, sampler, vocab: int, group=None):
+        import torch
+        import torch.distributed as dist
+        super().__init__(sampler, vocab, group)
+        mine = sampler.peer_setup(self.world, self.rank)
+        n = len(mine)
+        local = torch.tensor(list(mine), dtype=torch.uint8)
+        if dist.is_initialized() and dist.get_backend(group) == "nccl":
+            local = local.cuda(sampler.device)
+        everyone = gather_records(local.view(1, n), group)  # [world, 1, n], rank order
+        sampler.peer_connect(bytes(everyone.view(-1).cpu().tolist()))
+
+    def sample(self, logits_shard, hist_ids, hist_offsets, uniforms, params, tokens,
+               flags=None, stream=None) -> None:
+        import torch
+        rows, width = int(logits_shard.shape[0]), int(logits_shard.shape[1])
+        if width != self.width or width == 0:
+            raise ValueError(f"rank {self.rank} holds columns [{self.col_begin}, {self.col_end}),"
+                             f" got {width}")
+        cur = stream if stream is not None else torch.cuda.current_stream(logits_shard.device)
+        self.sampler.shard_push_peer_device(logits_shard, self.vocab, self.col_begin, hist_ids,
+                                            hist_offsets, params, cur)
+        self.sampler.shard_merge_peer_device(rows, self.vocab, uniforms, params, tokens, flags, cur)

@@ -151,3 +151,95 @@ def test_shard_capacity_and_argument_errors(gpu_sampler):
     assert lib.ncb_vocab_shard_merge_device(h, P(recs), 17, 2, 100, P(u), ctypes.byref(ok),
                                             P(tok), None, None) == native.NCB_ERROR_CAPACITY
     assert lib.ncb_vocab_shard_record_bytes() == 1040
+
+
+@pytest.mark.parametrize("G", [2, 4])
+def test_peer_exchange_emulated_on_one_gpu(navlib, G):
+    """The peer-memory exchange with every shard's area on one GPU: all shards
+    push, then all merge, for three calls in a row (epochs, flags and acks)."""
+    import torch
+    from neuraval_b200.sampler import CudaTokenSampler
+    B, V = 12, 30000
+    samplers = [CudaTokenSampler(0, max_rows=16, max_vocab=V, max_history=512) for _ in range(G)]
+    ref = CudaTokenSampler(0, max_rows=16, max_vocab=V, max_history=512)
+    try:
+        handles = b"".join(s.peer_setup(G, g) for g, s in enumerate(samplers))
+        for s in samplers:
+            s.peer_connect(handles)
+        for call in range(3):
+            wl = workloads.zipf_ranked(B=B, V=V, H=64, seed=40 + call)
+            if call == 2:
+                wl = workloads.peaked_head(B=B, V=V, seed=43, greedy=True)
+            logits, hist, offs, u = to_dev(wl)
+            p = native.make_params(**wl["params"])
+            for g, s in enumerate(samplers):
+                lo, hi = sharding.vocab_range(V, G, g)
+                s.shard_push_peer_device(logits[:, lo:hi], V, lo, hist, offs, p)
+            outs = []
+            for s in samplers:
+                tok = torch.full((B,), -7, dtype=torch.int32, device="cuda")
+                fl = torch.zeros(B, dtype=torch.int32, device="cuda")
+                s.shard_merge_peer_device(B, V, u, p, tok, fl)
+                outs.append((tok, fl))
+            rt, rf, _ = run_gpu(ref, wl)
+            torch.cuda.synchronize()
+            for tok, fl in outs:
+                assert np.array_equal(tok.cpu().numpy(), rt), (G, call)
+                assert np.array_equal(fl.cpu().numpy().astype(np.uint32), rf), (G, call)
+    finally:
+        for s in samplers + [ref]:
+            s.close()
+
+
+def _peer_rank_main(rank, world, port):
+    import os
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from neuraval_b200.sampler import CudaTokenSampler
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        B, V = 16, 65536
+        s = CudaTokenSampler(rank, max_rows=B, max_vocab=V, max_history=256)
+        s2 = CudaTokenSampler(rank, max_rows=B, max_vocab=V, max_history=256)
+        peer = sharding.PeerVocabShardedSampler(s, V)
+        nccl = sharding.VocabShardedSampler(s2, V)
+        for call in range(4):
+            wl = workloads.zipf_ranked(B=B, V=V, H=128, seed=60 + call)
+            logits, hist, offs, u = to_dev(wl)
+            shard = logits[:, peer.col_begin:peer.col_end].contiguous()
+            p = native.make_params(**wl["params"])
+            t1 = torch.empty(B, dtype=torch.int32, device="cuda")
+            f1 = torch.zeros(B, dtype=torch.int32, device="cuda")
+            t2 = torch.empty_like(t1)
+            f2 = torch.zeros_like(f1)
+            peer.sample(shard, hist, offs, u, p, t1, f1)
+            nccl.sample(shard, hist, offs, u, p, t2, f2)
+            torch.cuda.synchronize()
+            assert torch.equal(t1, t2) and torch.equal(f1, f2), (rank, call)
+            if rank == 0:
+                with CudaTokenSampler(0, max_rows=B, max_vocab=V, max_history=256) as one:
+                    rt, rf, _ = run_gpu(one, wl)
+                assert np.array_equal(t1.cpu().numpy(), rt), call
+        torch.cuda.synchronize()
+        dist.barrier()
+        s.close()
+        s2.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_two_gpus():
+    import socket
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as so:
+        so.bind(("127.0.0.1", 0))
+        port = so.getsockname()[1]
+    mp.start_processes(_peer_rank_main, args=(2, port), nprocs=2, start_method="spawn", join=True)
