@@ -6,12 +6,16 @@ batch (Zipf-ranked logits, 1024-id histories, repetition 1.15, T 0.7, top-k 50,
 top-p 0.9), i.e. the C ABI call ncb_sample_rows_device on device-resident inputs.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload zipf_ranked|vocab_sharded|softmax_rows] [--exchange nccl|peer]
 
 N>1 runs under torch.distributed (one process per GPU, NCCL for the barrier and
 the max-over-ranks timing only): every rank samples its own batch (rows shard
 across GPUs with no data-path exchange), so scaling is weak.
 --impl reference times the reference's CPU sampler on the host: the C# code
 cannot run here (no .NET runtime), so its C restatement (oracle/) stands in.
+Other workloads: vocab_sharded (the 128 x 262144 batch with its vocabulary split
+over the GPUs, strong scaling) and softmax_rows (the row softmax of the 256 x
+128256 batch; its reference arm is the reference's own CUDA kernel).
 """
 from __future__ import annotations
 
