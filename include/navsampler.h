@@ -148,6 +148,23 @@ NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int rows, int 
                                            const NcbSamplerParams* params, int32_t* d_tokens,
                                            uint32_t* d_flags, float* d_probs, void* stream);
 
+/* The same five operations on host arrays, in place (LogitsProcessor.* take a
+ * float[]): rows are copied in through the handle's staging buffers, processed
+ * and copied back before returning. Histories are host CSR arrays. */
+NCB_API int ncb_logits_repetition_penalty(NcbSampler* sampler, float* h_logits, int rows,
+                                          int vocab, const int32_t* h_hist,
+                                          const int32_t* h_hist_offsets, float penalty);
+NCB_API int ncb_logits_frequency_presence_penalty(NcbSampler* sampler, float* h_logits, int rows,
+                                                  int vocab, const int32_t* h_hist,
+                                                  const int32_t* h_hist_offsets, float frequency,
+                                                  float presence);
+NCB_API int ncb_logits_temperature(NcbSampler* sampler, float* h_logits, int rows, int vocab,
+                                   float temperature);
+NCB_API int ncb_logits_filter_top_k(NcbSampler* sampler, float* h_logits, int rows, int vocab,
+                                    int top_k);
+NCB_API int ncb_logits_filter_top_p(NcbSampler* sampler, float* h_probs, int rows, int vocab,
+                                    float top_p, uint32_t* h_flags);
+
 /* ---- vocabulary shards -----------------------------------------------------
  * No counterpart in the reference (it samples on one CPU thread): a batch whose
  * vocabulary is split in contiguous column ranges over several GPUs (a

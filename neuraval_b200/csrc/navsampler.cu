@@ -70,7 +70,7 @@ struct NcbSampler {
   int max_smem_optin = 0;
   int max_dyn_smem = 0;  // dynamic shared memory a launch may request (opt-in minus static)
   int forced_splits = 0;  // NAVSAMPLER_SPLITS at creation (tuning only)
-  std::mutex mu;
+  std::recursive_mutex mu;  // host-array entry points call the device ones under it
   void* scratch = nullptr;
   nvs::Scratch s{};
   nvs::FvScratch fv{};
@@ -382,6 +382,40 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, false, 0);
 }
 
+// Lazily sized staging buffers owned by the handle, for the host-array entry
+// points; caller holds h->mu and the device.
+static bool ensure_staging(NcbSampler* h, size_t nh, bool probs) {
+  if (!h->h_logits_dev) {
+    const size_t nl = (size_t)h->max_rows * h->max_vocab;
+    if (cudaMalloc(&h->h_logits_dev, nl * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->h_hoff_dev, ((size_t)h->max_rows + 1) * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&h->h_u_dev, (size_t)h->max_rows * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->h_tok_dev, (size_t)h->max_rows * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&h->h_flags_dev, (size_t)h->max_rows * sizeof(uint32_t)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return false;
+  }
+  if (nh > h->h_hist_cap) {
+    cudaFree(h->h_hist_dev);
+    h->h_hist_dev = nullptr;
+    const size_t cap = nh < 1024 ? 1024 : nh;
+    if (cudaMalloc(&h->h_hist_dev, cap * sizeof(int32_t)) != cudaSuccess) return false;
+    h->h_hist_cap = cap;
+  }
+  if (probs && !h->h_probs_dev &&
+      cudaMalloc(&h->h_probs_dev, (size_t)h->max_rows * h->max_vocab * sizeof(float)) != cudaSuccess)
+    return false;
+  return true;
+}
+
+// CSR offsets of `rows` host histories: start at 0, non-decreasing.
+static bool host_offsets_ok(const int32_t* hist, const int32_t* off, int rows) {
+  if (!off || off[0] != 0) return false;
+  for (int r = 0; r < rows; ++r)
+    if (off[r + 1] < off[r]) return false;
+  return off[rows] == 0 || hist != nullptr;
+}
+
 static int validate_sample_args(NcbSampler* h, const void* logits, int rows, int vocab,
                                 const void* hist, const void* hoff, const void* u,
                                 const NcbSamplerParams* prm, const void* tok) {
@@ -405,7 +439,7 @@ NCB_API int ncb_sample_rows_device(NcbSampler* h, const float* d_logits, int row
   int st = validate_sample_args(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms,
                                 params, d_tokens);
   if (st != NCB_OK) return set_status(st);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   st = launch_sample(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms, params,
@@ -425,32 +459,10 @@ NCB_API int ncb_sample_rows(NcbSampler* h, const float* h_logits, int rows, int 
   if (h_hist_offsets[0] != 0 || nh < 0 || (nh > 0 && !h_hist)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
   for (int r = 0; r < rows; ++r)
     if (h_hist_offsets[r + 1] < h_hist_offsets[r]) return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  // lazily sized staging buffers owned by the handle
-  if (!h->h_logits_dev) {
-    const size_t nl = (size_t)h->max_rows * h->max_vocab;
-    if (cudaMalloc(&h->h_logits_dev, nl * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&h->h_hoff_dev, ((size_t)h->max_rows + 1) * sizeof(int32_t)) != cudaSuccess ||
-        cudaMalloc(&h->h_u_dev, (size_t)h->max_rows * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&h->h_tok_dev, (size_t)h->max_rows * sizeof(int32_t)) != cudaSuccess ||
-        cudaMalloc(&h->h_flags_dev, (size_t)h->max_rows * sizeof(uint32_t)) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess)
-      return set_status(NCB_ERROR_ALLOC_FAILED);
-  }
-  if ((size_t)nh > h->h_hist_cap) {
-    cudaFree(h->h_hist_dev);
-    h->h_hist_dev = nullptr;
-    size_t cap = (size_t)nh < 1024 ? 1024 : (size_t)nh;
-    if (cudaMalloc(&h->h_hist_dev, cap * sizeof(int32_t)) != cudaSuccess)
-      return set_status(NCB_ERROR_ALLOC_FAILED);
-    h->h_hist_cap = cap;
-  }
-  if (h_probs && !h->h_probs_dev) {
-    if (cudaMalloc(&h->h_probs_dev, (size_t)h->max_rows * h->max_vocab * sizeof(float)) != cudaSuccess)
-      return set_status(NCB_ERROR_ALLOC_FAILED);
-  }
+  if (!ensure_staging(h, (size_t)nh, h_probs != nullptr)) return set_status(NCB_ERROR_ALLOC_FAILED);
   cudaStream_t s = h->host_stream;
   bool ok = cudaMemcpyAsync(h->h_logits_dev, h_logits, (size_t)rows * vocab * sizeof(float),
                             cudaMemcpyHostToDevice, s) == cudaSuccess;
@@ -496,7 +508,7 @@ NCB_API int ncb_logits_repetition_penalty_device(NcbSampler* h, float* d_logits,
   if (st != NCB_OK) return set_status(st);
   if (!d_hist_offsets || !(penalty > 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
   if (penalty == 1.0f || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:17-18
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   const size_t smem = (size_t)((vocab + 31) / 32) * 4;
   if ((int)smem > h->max_dyn_smem) return set_status(NCB_ERROR_CAPACITY);
@@ -516,7 +528,7 @@ NCB_API int ncb_logits_frequency_presence_penalty_device(NcbSampler* h, float* d
   if (!d_hist_offsets || frequency != frequency || presence != presence)
     return set_status(NCB_ERROR_INVALID_ARGUMENT);
   if ((frequency == 0.0f && presence == 0.0f) || rows == 0) return set_status(NCB_OK);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   const int h_cap = pow2_at_least(h->max_history > 0 ? h->max_history : 1);
   const size_t smem = (size_t)h_cap * 4;
@@ -532,7 +544,7 @@ NCB_API int ncb_logits_temperature_device(NcbSampler* h, float* d_logits, int ro
   if (st != NCB_OK) return set_status(st);
   if (!(temperature > 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
   if (temperature == 1.0f || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:44-45
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   const size_t n = (size_t)rows * vocab;
   const int grid = 4 * h->num_sms;
@@ -550,7 +562,7 @@ NCB_API int ncb_logits_filter_top_k_device(NcbSampler* h, float* d_logits, int r
   if (st != NCB_OK) return set_status(st);
   if (top_k <= 0) return set_status(NCB_ERROR_INVALID_ARGUMENT);
   if (top_k >= vocab || rows == 0) return set_status(NCB_OK);  // LogitsProcessor.cs:62-63
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   nvs::filter_top_k_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, vocab, top_k);
   return set_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
@@ -561,7 +573,7 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* h, float* d_probs, int ro
   int st = check_rows(h, d_probs, rows, vocab);
   if (st != NCB_OK) return set_status(st);
   if (!(top_p > 0.0f) || top_p > 1.0f) return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (top_p >= 1.0f || rows == 0) {  // LogitsProcessor.cs:84-85
@@ -832,7 +844,7 @@ NCB_API int ncb_vocab_shard_candidates_device(NcbSampler* h, const float* d_logi
   if (st != NCB_OK || rows == 0) return set_status(st);
   if (!d_records || (reinterpret_cast<uintptr_t>(d_records) & 3u) != 0u)
     return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   return set_status(launch_shard_candidates(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist,
@@ -854,7 +866,7 @@ NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, i
   const int K = prm->top_k < vocab ? prm->top_k : vocab;
   if (shards > nvs::VM_MAX_SHARDS || (!prm->greedy && K > nvs::TL_KMAX))
     return set_status(NCB_ERROR_CAPACITY);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   return set_status(launch_merge(h, static_cast<const uint32_t*>(d_records), shards, rows, vocab,
@@ -879,7 +891,7 @@ NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* h, int shards, int me, void* 
   if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
   if (shards < 1 || shards > nvs::PX_MAX || me < 0 || me >= shards || !handle_out || h->px_area)
     return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   const nvs::PeerLayout l = nvs::peer_layout(shards, h->max_rows);
@@ -909,7 +921,7 @@ NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* h, int shards, int me, void* 
 NCB_API int ncb_vocab_shard_peer_connect(NcbSampler* h, const void* handles) {
   if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
   if (!h->px_area || h->px_connected || !handles) return set_status(NCB_ERROR_INVALID_ARGUMENT);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   const char* hb = static_cast<const char*>(handles);
@@ -947,7 +959,7 @@ NCB_API int ncb_vocab_shard_push_peer_device(NcbSampler* h, const float* d_logit
   int st = check_shard_args(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist_offsets, prm);
   if (st != NCB_OK || rows == 0) return set_status(st);
   if (!h->px_connected) return set_status(NCB_ERROR_NOT_INITIALIZED);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -982,7 +994,7 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* h, int rows, int vocab
     return set_status(rows > h->max_rows ? NCB_ERROR_CAPACITY : NCB_ERROR_INVALID_ARGUMENT);
   const int K = prm->top_k < vocab ? prm->top_k : vocab;
   if (!prm->greedy && K > nvs::TL_KMAX) return set_status(NCB_ERROR_CAPACITY);
-  std::lock_guard<std::mutex> lk(h->mu);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   uint32_t* acks[nvs::PX_MAX] = {};
@@ -993,6 +1005,100 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* h, int rows, int vocab
   return set_status(launch_merge(h, reinterpret_cast<const uint32_t*>(h->px_area), h->px_shards,
                                  rows, vocab, d_uniforms, prm, d_tokens, d_flags, flags, acks,
                                  static_cast<cudaStream_t>(stream_)));
+}
+
+}  // extern "C"
+
+// ---- LogitsProcessor on host arrays ---------------------------------------------
+//
+// LogitsProcessor.* (LogitsProcessor.cs:8-114) operate in place on a float[]:
+// these copy the rows in through the handle's staging buffers, run the device
+// entry point, and copy them back.
+
+namespace {
+template <typename F>
+int host_logits_call(NcbSampler* h, float* h_x, int rows, int vocab, const int32_t* h_hist,
+                     const int32_t* h_off, bool need_hist, uint32_t* h_flags, F&& device_call) {
+  if (!h) return NCB_ERROR_NOT_INITIALIZED;
+  if (!h_x || rows < 0 || vocab <= 0) return NCB_ERROR_INVALID_ARGUMENT;
+  if (rows > h->max_rows || vocab > h->max_vocab) return NCB_ERROR_CAPACITY;
+  if (rows == 0) return NCB_OK;
+  if (need_hist && !host_offsets_ok(h_hist, h_off, rows)) return NCB_ERROR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return NCB_ERROR_INIT_FAILED;
+  const size_t nh = need_hist ? (size_t)h_off[rows] : 0;
+  if (!ensure_staging(h, nh, false)) return NCB_ERROR_ALLOC_FAILED;
+  cudaStream_t s = h->host_stream;
+  const size_t bytes = (size_t)rows * vocab * sizeof(float);
+  bool ok = cudaMemcpyAsync(h->h_logits_dev, h_x, bytes, cudaMemcpyHostToDevice, s) == cudaSuccess;
+  if (need_hist) {
+    ok = ok && cudaMemcpyAsync(h->h_hoff_dev, h_off, ((size_t)rows + 1) * sizeof(int32_t),
+                               cudaMemcpyHostToDevice, s) == cudaSuccess;
+    if (nh > 0)
+      ok = ok && cudaMemcpyAsync(h->h_hist_dev, h_hist, nh * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, s) == cudaSuccess;
+  }
+  if (!ok) return NCB_ERROR_COPY_FAILED;
+  const int st = device_call(h->h_logits_dev, s);
+  if (st != NCB_OK) return st;
+  ok = cudaMemcpyAsync(h_x, h->h_logits_dev, bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  if (h_flags)
+    ok = ok && cudaMemcpyAsync(h_flags, h->h_flags_dev, (size_t)rows * sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  if (!ok) return NCB_ERROR_COPY_FAILED;
+  return cudaStreamSynchronize(s) == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
+}
+}  // namespace
+
+extern "C" {
+
+NCB_API int ncb_logits_repetition_penalty(NcbSampler* h, float* h_logits, int rows, int vocab,
+                                          const int32_t* h_hist, const int32_t* h_hist_offsets,
+                                          float penalty) {
+  return set_status(host_logits_call(h, h_logits, rows, vocab, h_hist, h_hist_offsets, true,
+                                     nullptr, [&](float* d, cudaStream_t s) {
+    return ncb_logits_repetition_penalty_device(h, d, rows, vocab, h->h_hist_dev, h->h_hoff_dev,
+                                                penalty, s);
+  }));
+}
+
+NCB_API int ncb_logits_frequency_presence_penalty(NcbSampler* h, float* h_logits, int rows,
+                                                  int vocab, const int32_t* h_hist,
+                                                  const int32_t* h_hist_offsets, float frequency,
+                                                  float presence) {
+  return set_status(host_logits_call(h, h_logits, rows, vocab, h_hist, h_hist_offsets, true,
+                                     nullptr, [&](float* d, cudaStream_t s) {
+    return ncb_logits_frequency_presence_penalty_device(h, d, rows, vocab, h->h_hist_dev,
+                                                        h->h_hoff_dev, frequency, presence, s);
+  }));
+}
+
+NCB_API int ncb_logits_temperature(NcbSampler* h, float* h_logits, int rows, int vocab,
+                                   float temperature) {
+  if (!(temperature > 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  return set_status(host_logits_call(h, h_logits, rows, vocab, nullptr, nullptr, false, nullptr,
+                                     [&](float* d, cudaStream_t s) {
+    return ncb_logits_temperature_device(h, d, rows, vocab, temperature, s);
+  }));
+}
+
+NCB_API int ncb_logits_filter_top_k(NcbSampler* h, float* h_logits, int rows, int vocab,
+                                    int top_k) {
+  if (top_k <= 0) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  return set_status(host_logits_call(h, h_logits, rows, vocab, nullptr, nullptr, false, nullptr,
+                                     [&](float* d, cudaStream_t s) {
+    return ncb_logits_filter_top_k_device(h, d, rows, vocab, top_k, s);
+  }));
+}
+
+NCB_API int ncb_logits_filter_top_p(NcbSampler* h, float* h_probs, int rows, int vocab,
+                                    float top_p, uint32_t* h_flags) {
+  if (!(top_p > 0.0f) || top_p > 1.0f) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  return set_status(host_logits_call(h, h_probs, rows, vocab, nullptr, nullptr, false, h_flags,
+                                     [&](float* d, cudaStream_t s) {
+    return ncb_logits_filter_top_p_device(h, d, rows, vocab, top_p, h->h_flags_dev, s);
+  }));
 }
 
 }  // extern "C"

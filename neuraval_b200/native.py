@@ -80,6 +80,11 @@ SIGNATURES = {
     "ncb_vocab_shard_merge_peer_device": (_I, [_P, _I, _I, _P, ctypes.POINTER(NcbSamplerParams),
                                                _P, _P, _P]),
     "ncb_softmax_rows_device": (_I, [_P, _P, _I, _I, _P]),
+    "ncb_logits_repetition_penalty": (_I, [_P, _P, _I, _I, _P, _P, _F]),
+    "ncb_logits_frequency_presence_penalty": (_I, [_P, _P, _I, _I, _P, _P, _F, _F]),
+    "ncb_logits_temperature": (_I, [_P, _P, _I, _I, _F]),
+    "ncb_logits_filter_top_k": (_I, [_P, _P, _I, _I, _I]),
+    "ncb_logits_filter_top_p": (_I, [_P, _P, _I, _I, _F, _P]),
     "ncb_sampler_last_status": (_I, []),
     "ncb_sampler_status_message": (ctypes.c_char_p, [_I]),
 }

@@ -114,3 +114,44 @@ def test_filter_top_p_matches_oracle(gpu_sampler, oracle, V):
             _, want, tie = oracle.filter_top_p(p[r], top_p)
             assert bool(gfl[r] & 0x4) == bool(tie), (top_p, r)
             assert np.array_equal(got[r], want), (top_p, r)
+
+
+def test_host_array_entry_points_match_device_ones(gpu_sampler):
+    """ncb_logits_* on host arrays give the bits of the device entry points."""
+    import ctypes
+    import torch
+    from neuraval_b200 import native
+    lib = native.load()
+    h = gpu_sampler._h
+    rng = np.random.default_rng(91)
+    B, V = 5, 7001
+    x = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    hist = rng.integers(-5, V + 5, size=40).astype(np.int32)
+    offs = np.array([0, 8, 8, 20, 31, 40], np.int32)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    T = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def both(host_call, dev_call):
+        a = x.copy()
+        assert host_call(a) == 0
+        d = torch.from_numpy(x).cuda()
+        assert dev_call(d) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(a, d.cpu().numpy())
+
+    dh, do = torch.from_numpy(hist).cuda(), torch.from_numpy(offs).cuda()
+    both(lambda a: lib.ncb_logits_repetition_penalty(h, P(a), B, V, P(hist), P(offs), 1.3),
+         lambda d: lib.ncb_logits_repetition_penalty_device(h, T(d), B, V, T(dh), T(do), 1.3, None))
+    both(lambda a: lib.ncb_logits_frequency_presence_penalty(h, P(a), B, V, P(hist), P(offs),
+                                                             0.4, 0.2),
+         lambda d: lib.ncb_logits_frequency_presence_penalty_device(h, T(d), B, V, T(dh), T(do),
+                                                                    0.4, 0.2, None))
+    both(lambda a: lib.ncb_logits_temperature(h, P(a), B, V, 0.7),
+         lambda d: lib.ncb_logits_temperature_device(h, T(d), B, V, 0.7, None))
+    both(lambda a: lib.ncb_logits_filter_top_k(h, P(a), B, V, 37),
+         lambda d: lib.ncb_logits_filter_top_k_device(h, T(d), B, V, 37, None))
+    p = np.exp(x - x.max(axis=1, keepdims=True))
+    x = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+    both(lambda a: lib.ncb_logits_filter_top_p(h, P(a), B, V, 0.9, None),
+         lambda d: lib.ncb_logits_filter_top_p_device(h, T(d), B, V, 0.9, None, None))
+    assert lib.ncb_logits_temperature(h, P(x.copy()), B, V, 0.0) == native.NCB_ERROR_INVALID_ARGUMENT
