@@ -53,7 +53,8 @@ def parse():
                     help="vocab_sharded: records exchanged by an NCCL all-gather, or through "
                          "peer memory by the shard kernel itself")
     ap.add_argument("--workload", default="zipf_ranked",
-                    choices=["zipf_ranked", "vocab_sharded", "softmax_rows"],
+                    choices=["zipf_ranked", "peaked_head", "zipf_history_nucleus",
+                             "high_entropy_nucleus", "vocab_sharded", "softmax_rows"],
                     help="zipf_ranked: the headline (rows shard over GPUs); vocab_sharded: "
                          "128 x 262144, vocabulary split over GPUs; softmax_rows: row softmax "
                          "of the 256 x 128256 logits batch")
@@ -67,20 +68,19 @@ def dist_env():
     return rank, world, local
 
 
-def workload(rank=0):
-    """The headline batch; rank r > 0 of a multi-GPU run gets its own rows
-    (same generator, another seed)."""
+def workload(rank=0, name="zipf_ranked"):
+    """The batch of a sampling workload (the headline by default); rank r > 0 of
+    a multi-GPU run gets its own rows (same generator, another seed)."""
     from neuraval_b200 import workloads
-    return workloads.zipf_ranked() if rank == 0 else workloads.zipf_ranked(seed=3 + 1000 * rank)
+    gen = workloads.WORKLOADS[name]
+    return gen() if rank == 0 else gen(seed=1000 * rank + 7)
 
 
 def config_of(wl, extra=None):
     B, V = wl["logits"].shape
     H = int(wl["hist_offsets"][-1] // B)
     c = {"workload": wl["name"], "B": B, "V": V, "history_per_row": H,
-         "top_k": wl["params"]["top_k"], "top_p": wl["params"]["top_p"],
-         "temperature": wl["params"]["temperature"],
-         "repetition_penalty": wl["params"]["repetition_penalty"],
+         **{k: v for k, v in wl["params"].items()},
          "uniforms": "one seeded u in [0,1) per row",
          "l2": f"inputs larger than L2: {NBUF} copies of the batch rotated across steps"}
     if extra:
@@ -174,8 +174,8 @@ def cpu_baseline(wl, seconds):
     p = pyoracle.make_params(**wl["params"])
     offs = np.asarray(wl["hist_offsets"], np.int64)
     B = wl["logits"].shape[0]
-    # single thread on 16 rows
-    sub = 16
+    # single thread on up to 16 rows
+    sub = min(16, B)
     t0 = time.perf_counter()
     pyoracle.sample_rows(wl["logits"][:sub], wl["hist_ids"][: offs[sub]], offs[: sub + 1],
                          wl["uniforms"][:sub], p, exp_mode=pyoracle.EXP_GLIBC, threads=1)
@@ -190,12 +190,26 @@ def cpu_baseline(wl, seconds):
     return rows / dt, threads, f"{rows} rows ({rows // B} full batches of {B}) in {dt:.1f} s", one
 
 
+def kernels_of(params, V):
+    """The kernels one sampling call launches for these parameters (the
+    dispatch of ncb_sample_rows_device): a name for the timed pair and the
+    number of launches per step."""
+    k = params.get("top_k", 0) or 0
+    if params.get("greedy"):
+        return "greedy_kernel", 1
+    if 0 < k < V and k <= 64:
+        return "topk_ldg_kernel (+ its fix-up launch, timed together)", 2
+    if 0 < k < V and k <= 1024:
+        return "topk_kernel (+ its fix-up launch, timed together)", 2
+    return "fullvocab_kernel", 1
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     if args.workload == "softmax_rows":
         return run_softmax_reference(args)
-    wl = workload()
+    wl = workload(0, args.workload)
     from oracle import pyoracle
     pyoracle.build()
     threads = os.cpu_count() or 1
@@ -265,17 +279,18 @@ def run_rows(args, rank, world, dev):
     from neuraval_b200 import native, sharding, workloads
     from neuraval_b200.sampler import CudaTokenSampler
 
-    wl = workload(rank)
+    wl = workload(rank, args.workload)
     B, V = wl["logits"].shape
     H = int(wl["hist_offsets"][-1] // B)
     params = native.make_params(**wl["params"])
     sampler = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=V, max_history=H)
+    nbuf = max(NBUF, -(-2 * L2_BYTES // max(1, B * V * 4)))  # rotated copies span 2 x L2
 
     bufs = []
-    for i in range(NBUF):
+    for i in range(nbuf):
         lg = torch.from_numpy(wl["logits"]).to(dev)
         if i:
-            lg = lg.roll(i, dims=0)  # distinct copies, same workload
+            lg = lg.roll(i, dims=0) if B > 1 else lg.roll(i * 97, dims=1)  # distinct copies
         bufs.append(lg.contiguous())
     hist = torch.from_numpy(wl["hist_ids"]).to(dev)
     offs = torch.from_numpy(wl["hist_offsets"]).to(dev)
@@ -284,7 +299,7 @@ def run_rows(args, rank, world, dev):
     flags = torch.empty(B, dtype=torch.int32, device=dev)
 
     def step(i, stream):
-        sampler.sample_rows_device(bufs[i % NBUF], hist, offs, u, params, tokens, flags,
+        sampler.sample_rows_device(bufs[i % nbuf], hist, offs, u, params, tokens, flags,
                                    None, stream)
 
     cur = torch.cuda.current_stream(dev)
@@ -356,19 +371,23 @@ def run_rows(args, rank, world, dev):
         peak, peak_kind = measured_peak()
         bytes_per_launch = B * workloads.bytes_per_row(V, H)
         achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
+        kernel, launches = kernels_of(wl["params"], V)
         out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
                "config": config_of(wl, {"parallelism": f"rows sharded, {world} GPU(s) x {B} rows"
-                                                       ", no exchange"}),
+                                                       ", no exchange",
+                                        "l2": f"inputs larger than L2: {nbuf} copies of the "
+                                              "batch rotated across steps"}),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "peak_source": peak_kind,
-                            "traffic": profiled_traffic(),
-                            "kernel": "topk_ldg_kernel (+ its fix-up launch, timed together)",
+                            "traffic": profiled_traffic() if wl["name"].startswith("zipf_ranked")
+                            else None,
+                            "kernel": kernel,
                             "algorithmic_bytes_per_launch": bytes_per_launch},
                "e2e": e2e,
-               "gpu_launches": 2 * args.steps,
+               "gpu_launches": launches * args.steps,
                "eager_value": world * B * args.steps / (eager_ms / 1e3),
                "timing": "CUDA events around one replay of a CUDA graph holding the K steps; "
                          "max over ranks",
