@@ -201,7 +201,7 @@ def kernels_of(params, V):
         return "topk_ldg_kernel (+ its fix-up launch, timed together)", 2
     if 0 < k < V and k <= 1024:
         return "topk_kernel (+ its fix-up launch, timed together)", 2
-    return "fullvocab_kernel", 1
+    return "nucleus_kernel (+ its full-sort fix-up launch, timed together)", 2
 
 
 def run_reference(args, rank, world):

@@ -56,7 +56,7 @@ extern "C" {
                                          unstable sort (TokenSampler.cs:95) picks the id */
 #define NCB_FLAG_NONFINITE 0x8u       /* NaN/+inf value or no finite maximum: token -1 */
 #define NCB_FLAG_EXP_SLOW 0x10u       /* a weight needed the double-double exp path */
-#define NCB_FLAG_BAD_HISTORY 0x20u    /* row history longer than the handle's max: token -1 */
+#define NCB_FLAG_BAD_HISTORY 0x20u    /* frequency counting over a history longer than the handle's max: token -1 */
 #define NCB_FLAG_TIES_OVERFLOW 0x40u  /* ncb_sample_rows_noalloc_device and vocabulary-shard
                                          merges only: ties at the k-th value exceed the
                                          candidate buffers: token -1 */
@@ -133,8 +133,8 @@ NCB_API int ncb_sample_rows(NcbSampler* sampler, const float* h_logits, int rows
  *     shared-memory limits; make that first call before any stream capture.
  *   - Serves greedy rows and top-k <= 64 only; other options return
  *     NCB_ERROR_CAPACITY, as do rows > 1024 and vocab > 2^24. A row whose
- *     frequency/presence counting needs more than 4096 history ids comes back
- *     as token -1 with NCB_FLAG_BAD_HISTORY.
+ *     frequency counting needs more than 4096 history ids comes back as
+ *     token -1 with NCB_FLAG_BAD_HISTORY.
  *   - Every call reuses the same array (the parts that must start at zero are
  *     cleared on `stream` at the start of each call): calls that overlap on the
  *     GPU, from any stream or thread, race and corrupt each other's results.
@@ -264,6 +264,20 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* sampler, int rows, int
  * asynchronous on `stream`. */
 NCB_API int ncb_softmax_rows_device(const float* d_in, float* d_out, int rows, int cols,
                                     void* stream);
+
+/* ---- diagnostics ----------------------------------------------------------
+ * Rows this handle has redone on the exact full-sort kernel since it was
+ * created: top-k rows whose ties overflowed the candidate buffers, and
+ * full-vocabulary rows the bucketed kernel handed over (a running-sum
+ * estimate outside its margin, a very large bucket of equal-looking values).
+ * Synchronises the device. */
+NCB_API int ncb_sampler_full_sort_rows(NcbSampler* sampler, uint64_t* out_rows);
+
+/* Largest distance, in float steps, between the fast exponential the bucketed
+ * kernel estimates with and the correctly rounded exp over every float x in
+ * [x_lo, x_hi] (x_lo <= x_hi <= 0). The kernel relies on at most 21 steps on
+ * [-17, 0]. Synchronous; runs on the current device. */
+NCB_API int ncb_fast_exp_max_steps(float x_lo, float x_hi, uint32_t* out_steps);
 
 /* ---- status --------------------------------------------------------------- */
 /* ncb_cuda_last_status / ncb_cuda_status_message (navcuda.cu:982-1001). */

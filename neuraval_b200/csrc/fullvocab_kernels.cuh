@@ -581,7 +581,10 @@ __global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(const __
     for (int i = 0; i < n; ++i) {
       const int row = s_list[i];
       fullvocab_row<kCounts>(a, f, K, row, smem);
-      if (threadIdx.x == 0) a.s.fixup[row] = 0u;
+      if (threadIdx.x == 0) {
+        a.s.fixup[row] = 0u;
+        if (a.s.stats) atomicAdd(a.s.stats, 1u);
+      }
       __syncthreads();
     }
   }

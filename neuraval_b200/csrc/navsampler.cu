@@ -18,6 +18,7 @@
 
 #include "fullvocab_kernels.cuh"
 #include "logits_ops.cuh"
+#include "nucleus_kernel.cuh"
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
 #include "topk_ldg_kernel.cuh"
@@ -164,6 +165,8 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::greedy_kernel<true, true>);
   set((const void*)nvs::greedy_kernel<false, true>);
   set((const void*)nvs::vocab_merge_kernel);
+  set((const void*)nvs::nucleus_kernel<true>);
+  set((const void*)nvs::nucleus_kernel<false>);
   set((const void*)nvs::fullvocab_kernel<true>);
   set((const void*)nvs::fullvocab_kernel<false>);
   set((const void*)nvs::fullvocab_fixup_kernel<true>);
@@ -181,6 +184,39 @@ NCB_API int ncb_sampler_params_validate(const NcbSamplerParams* params) {
 }
 
 NCB_API int ncb_sampler_last_status(void) { return g_last_status.load(); }
+
+NCB_API int ncb_sampler_full_sort_rows(NcbSampler* h, uint64_t* out_rows) {
+  if (!h || !out_rows) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  uint32_t n = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&n, h->s.stats, sizeof(n), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_status(NCB_ERROR_COPY_FAILED);
+  *out_rows = n;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_fast_exp_max_steps(float x_lo, float x_hi, uint32_t* out_steps) {
+  if (!out_steps || !(x_lo <= x_hi) || !(x_hi <= 0.0f)) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  uint32_t* d = nullptr;
+  if (cudaMalloc(&d, sizeof(uint32_t)) != cudaSuccess) return set_status(NCB_ERROR_ALLOC_FAILED);
+  int st = NCB_OK;
+  if (cudaMemset(d, 0, sizeof(uint32_t)) != cudaSuccess) st = NCB_ERROR_LAUNCH_FAILED;
+  // every float in [x_lo, x_hi]: for x <= 0 the bit pattern grows as x falls,
+  // from 0x80000000 (-0)
+  const uint32_t k0 = x_hi == 0.0f ? 0x80000000u : __builtin_bit_cast(uint32_t, x_hi);
+  const uint32_t k1 = __builtin_bit_cast(uint32_t, x_lo);
+  if (st == NCB_OK) {
+    nvs::fast_exp_steps_kernel<<<148 * 8, 256>>>(k0, k1, d);
+    if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+      st = NCB_ERROR_LAUNCH_FAILED;
+  }
+  if (st == NCB_OK && cudaMemcpy(out_steps, d, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    st = NCB_ERROR_COPY_FAILED;
+  cudaFree(d);
+  return set_status(st);
+}
 
 NCB_API const char* ncb_sampler_status_message(int status) {
   switch (status) {
@@ -244,6 +280,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   const size_t o_er = carve(sizeof(uint32_t));
   const size_t o_fx = carve((size_t)max_rows * sizeof(uint32_t));
   const size_t o_px = carve(4 * sizeof(uint32_t));
+  const size_t o_st = carve(4 * sizeof(uint32_t));
   const nvs::FvLayout fl = nvs::fv_layout(max_rows, max_vocab);
   const size_t o_fv = carve(fl.total_bytes);
   if (cudaMalloc(&h->scratch, off) != cudaSuccess) {
@@ -261,6 +298,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->s.error_word = reinterpret_cast<uint32_t*>(b + o_er);
   h->s.fixup = reinterpret_cast<uint32_t*>(b + o_fx);
   h->s.px_ticket = reinterpret_cast<uint32_t*>(b + o_px);
+  h->s.stats = reinterpret_cast<uint32_t*>(b + o_st);
   h->fv = nvs::fv_carve(b + o_fv, fl);
   // tickets/rowstate/error word must start at zero; the kernels restore zero
   if (!raise_smem_limits(h->max_smem_optin) || cudaMemset(h->scratch, 0, off) != cudaSuccess ||
@@ -378,7 +416,10 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     return fst;
   }
 
-  // Full-vocabulary nucleus (no effective top-k) and very large top-k.
+  // Full-vocabulary nucleus (no effective top-k) and very large top-k: the
+  // bucketed kernel, with the full-sort kernel for the rows it hands over and
+  // for calls that want the probabilities written.
+  if (!d_probs) return nvs::launch_nucleus(h->fv, a, rows, K, h->max_dyn_smem, stream);
   return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, false, 0);
 }
 

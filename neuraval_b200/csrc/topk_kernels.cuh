@@ -42,6 +42,7 @@ struct Scratch {
   uint32_t* fixup;      // [max_rows]  1: row must be redone on the full-vocabulary path
   uint32_t* px_ticket;  // [4] peer exchange: push CTAs, failed push waits, merge CTAs (zero
                         // between launches), epoch of the last call
+  uint32_t* stats;      // [1] rows redone by the full-sort kernel (null: not counted)
 };
 
 struct SampleArgs {
@@ -87,6 +88,10 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
   P.rep = (P.pen != 1.0f) && H > 0;
   P.cnt = kCounts && (P.freq != 0.0f || P.pres != 0.0f) && H > 0;
   if (!P.rep && !P.cnt) return true;
+  // occurrence counts matter only through cnt * frequency: with a zero
+  // frequency (either sign) cnt * f is that zero for every count, so the ids
+  // are neither collected nor sorted (P.hn stays 0, every count reads 0)
+  const bool counting = kCounts && P.cnt && P.freq != 0.0f;
   const int words = ((c1 - c0 + 31) >> 5) + 1;  // one spare word for 4-id windows
   for (int i = threadIdx.x; i < words; i += blockDim.x) bitmap[i] = 0u;
   if (threadIdx.x == 0) *s_hn = 0;
@@ -96,7 +101,7 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
     if (id >= c0 && id < c1) {
       const int rel = id - c0;
       atomicOr(&bitmap[rel >> 5], 1u << (rel & 31));
-      if (kCounts && P.cnt) {
+      if (counting) {
         const int slot = atomicAdd(s_hn, 1);
         if (slot < a.h_cap) hsorted[slot] = id;
       }
@@ -104,7 +109,7 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
   }
   __syncthreads();
   bool ok = true;
-  if (kCounts && P.cnt) {
+  if (counting) {
     const int n = *s_hn;
     if (n > a.h_cap) {
       ok = false;

@@ -85,6 +85,8 @@ SIGNATURES = {
     "ncb_logits_temperature": (_I, [_P, _P, _I, _I, _F]),
     "ncb_logits_filter_top_k": (_I, [_P, _P, _I, _I, _I]),
     "ncb_logits_filter_top_p": (_I, [_P, _P, _I, _I, _F, _P]),
+    "ncb_sampler_full_sort_rows": (_I, [_P, ctypes.POINTER(ctypes.c_uint64)]),
+    "ncb_fast_exp_max_steps": (_I, [_F, _F, ctypes.POINTER(ctypes.c_uint32)]),
     "ncb_sampler_last_status": (_I, []),
     "ncb_sampler_status_message": (ctypes.c_char_p, [_I]),
 }

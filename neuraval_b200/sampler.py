@@ -173,5 +173,20 @@ class CudaTokenSampler:
             self._h, _ptr(probs), int(probs.shape[0]), int(probs.shape[1]),
             ctypes.c_float(top_p), _ptr(flags), _stream_ptr(stream)), "filter_top_p")
 
+    def full_sort_rows(self) -> int:
+        """Rows this handle redid on the exact full-sort kernel (synchronises)."""
+        n = ctypes.c_uint64(0)
+        check(self._lib.ncb_sampler_full_sort_rows(self._h, ctypes.byref(n)), "full_sort_rows")
+        return int(n.value)
 
-__all__ = ["CudaTokenSampler", "NcbSamplerParams", "make_params", "native"]
+
+def fast_exp_max_steps(x_lo: float, x_hi: float) -> int:
+    """Largest float-step distance between the bucketed kernel's fast exp
+    estimate and the correctly rounded exp over every float in [x_lo, x_hi]."""
+    out = ctypes.c_uint32(0)
+    check(native.load().ncb_fast_exp_max_steps(ctypes.c_float(x_lo), ctypes.c_float(x_hi),
+                                               ctypes.byref(out)), "fast_exp_max_steps")
+    return int(out.value)
+
+
+__all__ = ["CudaTokenSampler", "NcbSamplerParams", "make_params", "native", "fast_exp_max_steps"]
