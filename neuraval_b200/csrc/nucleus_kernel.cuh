@@ -39,8 +39,17 @@
 
 namespace nvs {
 
-constexpr int NC_THREADS = 1024;
-constexpr int NC_NB = 4096;             // value buckets
+#ifndef NC_THREADS_PER_CTA
+#define NC_THREADS_PER_CTA 1024
+#endif
+#ifndef NC_BUCKETS
+#define NC_BUCKETS 4096
+#endif
+#ifndef NC_CTAS_PER_SM
+#define NC_CTAS_PER_SM 1
+#endif
+constexpr int NC_THREADS = NC_THREADS_PER_CTA;
+constexpr int NC_NB = NC_BUCKETS;       // value buckets
 constexpr int NC_PER = NC_NB / NC_THREADS;
 constexpr int NC_WARPS = NC_THREADS / 32;
 constexpr int NC_SORT_WARP = 256;       // buckets up to this size are sorted by one warp
@@ -50,6 +59,10 @@ constexpr uint32_t NC_SPECIAL = 0x8000u;  // elements gathered, sorted and walke
 constexpr uint32_t NC_EXCL = 0x4000u;     // after the top-k cut
 constexpr uint32_t NC_UNIFORM = 0x2000u;  // every weight rounds to the same grid units
 constexpr uint32_t NC_GATHER = 0x1000u;   // may hold the cutoff or the draw: gathered too
+constexpr uint32_t NC_STRADDLE = 0x0800u; // one half grid point inside: units by two x thresholds
+constexpr uint32_t NC_TIEF = 0x0400u;     // straddling bucket with weights exactly at the half point
+constexpr uint32_t NC_MULTI = 0x0200u;    // several half points inside: gathered, units per element
+constexpr int NC_TIES = 64;               // such weights per row
 constexpr uint32_t NC_EMASK = 0x00FFu;
 constexpr uint32_t NC_QMAX = 1u << 23;  // a normal bucket's grid units stay below this
 constexpr int NC_QCAP = NC_NB;          // weights queued for the exact exp in one pass
@@ -63,13 +76,16 @@ constexpr int NC_FAST_EXP_ULPS = 21;
 
 struct NcSmem {
   uint32_t* pos;    // [NB+1] first sorted position of each bucket
-  uint32_t* cur;    // [NB] counts, then gather cursors
+  uint32_t* cur;    // [NB+1] counts, then gather cursors (entry NB counts the values
+                    // below e^-17 relative to the maximum, which never matter)
   uint32_t* qs;     // [NB] grid units of a normal bucket, then their exclusive prefix
+  uint32_t* kq;     // [NB] straddling bucket: units of a weight below its half point;
+                    // multi bucket: offset of its elements in the per-element pass
   float* send;      // [NB] exact running sum after each bucket
   float* regS;      // [NB+1] running sum at the start of each region
   uint16_t* splist; // [NB] special non-empty buckets, ascending
   uint16_t* soff;   // [NB] offset of each special bucket's elements in the walk's stage
-  uint16_t* bk;     // [NB] binade of a normal bucket | NC_* flags
+  uint16_t* bk;     // [NB+1] binade of a normal bucket | NC_* flags (entry NB: 0)
   uint32_t* tie;    // [NB/32] buckets holding an exact half (made special)
   uint32_t* gat;    // [NB/32] buckets to gather in the current pass
   uint32_t* bitmap;
@@ -77,7 +93,8 @@ struct NcSmem {
 };
 
 inline size_t nc_smem_bytes(int bm_words, int h_cap) {
-  return (size_t)(NC_NB + 1) * 4 + (size_t)NC_NB * 4 * 3 + (size_t)(NC_NB + 1) * 4 +
+  return (size_t)(NC_NB + 1) * 4 + (size_t)(NC_NB + 4) * 4 + (size_t)NC_NB * 4 * 3 +
+         (size_t)(NC_NB + 1) * 4 + 8 +
          (size_t)NC_NB * 2 * 3 + (size_t)NC_NB / 32 * 4 * 2 + 64 +
          (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
@@ -86,8 +103,9 @@ __device__ __forceinline__ NcSmem nc_carve(unsigned char* smem, int bm_words) {
   NcSmem s;
   unsigned char* p = smem;
   s.pos = reinterpret_cast<uint32_t*>(p); p += (NC_NB + 1) * 4;
-  s.cur = reinterpret_cast<uint32_t*>(p); p += NC_NB * 4;
+  s.cur = reinterpret_cast<uint32_t*>(p); p += (NC_NB + 4) * 4;
   s.qs = reinterpret_cast<uint32_t*>(p); p += NC_NB * 4;
+  s.kq = reinterpret_cast<uint32_t*>(p); p += NC_NB * 4;
   s.send = reinterpret_cast<float*>(p); p += NC_NB * 4;
   s.regS = reinterpret_cast<float*>(p); p += (NC_NB + 1) * 4;
   s.tie = reinterpret_cast<uint32_t*>(p); p += NC_NB / 32 * 4;
@@ -95,7 +113,7 @@ __device__ __forceinline__ NcSmem nc_carve(unsigned char* smem, int bm_words) {
   s.bitmap = reinterpret_cast<uint32_t*>(p); p += (size_t)bm_words * 4;
   s.splist = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2;
   s.soff = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2;
-  s.bk = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2;
+  s.bk = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2 + 8;
   p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
   s.hsorted = reinterpret_cast<int32_t*>(p);
   return s;
@@ -160,6 +178,48 @@ __device__ __forceinline__ void nc_stream(const float* lrow, int V, const Penalt
   }
 }
 
+// nc_stream with the aligned body handed over four values at a time:
+// f4(v0, v1, v2, v3, c) for columns c..c+3, f(v, c) for the unaligned ends.
+template <typename F, typename F4>
+__device__ __forceinline__ void nc_stream4(const float* lrow, int V, const Penalty& P, float scale,
+                                           F&& f, F4&& f4) {
+  const bool pen = P.rep || P.cnt;
+  auto val = [&](float l, bool member, int c) {
+    return canon(__fmul_rn(member ? nc_adjust_member(P, l, c) : l, scale));
+  };
+  auto bit = [&](int c) { return pen && ((P.bitmap[c >> 5] >> (c & 31)) & 1u); };
+  const int head = (int)(((16u - ((uint32_t)(uintptr_t)lrow & 15u)) & 15u) >> 2);
+  const int a0 = head < V ? head : V;
+  const int n4 = (V - a0) >> 2;
+  const int a1 = a0 + 4 * n4;
+  for (int c = threadIdx.x; c < a0; c += NC_THREADS) f(val(lrow[c], bit(c), c), c);
+  for (int c = a1 + threadIdx.x; c < V; c += NC_THREADS) f(val(lrow[c], bit(c), c), c);
+  const float4* body = reinterpret_cast<const float4*>(lrow + a0);
+  for (int q0 = threadIdx.x; q0 < n4; q0 += NC_THREADS * NC_INFLIGHT) {
+    float4 buf[NC_INFLIGHT];
+#pragma unroll
+    for (int u = 0; u < NC_INFLIGHT; ++u) {
+      const int q = q0 + u * NC_THREADS;
+      if (q < n4) buf[u] = __ldg(body + q);
+    }
+#pragma unroll
+    for (int u = 0; u < NC_INFLIGHT; ++u) {
+      const int q = q0 + u * NC_THREADS;
+      if (q < n4) {
+        const int c = a0 + 4 * q;
+        uint32_t bits = 0u;
+        if (pen) {
+          const int w = c >> 5, sh = c & 31;
+          const uint64_t win = (uint64_t)P.bitmap[w] | ((uint64_t)P.bitmap[w + 1] << 32);
+          bits = (uint32_t)(win >> sh) & 0xFu;
+        }
+        f4(val(buf[u].x, bits & 1u, c), val(buf[u].y, bits & 2u, c + 1),
+           val(buf[u].z, bits & 4u, c + 2), val(buf[u].w, bits & 8u, c + 3), c);
+      }
+    }
+  }
+}
+
 // Grid units of one weight by the correctly rounded exp (the fast estimate was
 // too close to a half grid point): returns false for an exact half.
 __device__ __noinline__ bool nc_units_exact(float x, float sc, uint32_t* q, int* slow_flag) {
@@ -186,14 +246,14 @@ __device__ __forceinline__ T nc_block_scan(T v, T* s_tmp, T* total) {
   if (lane == 31) s_tmp[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    const T wv = s_tmp[lane];  // NC_WARPS == 32
+    const T wv = lane < NC_WARPS ? s_tmp[lane] : T(0);
     T wi = wv;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const T o = __shfl_up_sync(0xffffffffu, wi, d);
       if (lane >= d) wi += o;
     }
-    s_tmp[lane] = wi - wv;
+    if (lane < NC_WARPS) s_tmp[lane] = wi - wv;
     if (lane == 31) s_tmp[32] = wi;
   }
   __syncthreads();
@@ -324,6 +384,62 @@ __device__ float nc_warp_exact_run(float* ws, int n, float S) {
   return S;
 }
 
+// Smallest float x < 0 whose correctly rounded exp is >= w (gt = false) or > w
+// (gt = true), by steps of one float from x0 (close to log w); false when the
+// steps run out. exp_cr is monotone, so every x below the result rounds below.
+__device__ __noinline__ bool nc_exp_threshold(float w, bool gt, float x0, float* out, int* slow_flag) {
+  auto ok = [&](float x) {
+    bool sl = false;
+    const float e = exp_cr(x, sl);
+    if (sl) *slow_flag = 1;
+    return gt ? e > w : e >= w;
+  };
+  // for x < 0 the next float up (toward 0) has the bit pattern minus one
+  float x = x0;
+  if (!(x < -0x1p-100f)) return false;
+  if (ok(x)) {
+    for (int i = 0; i < 64; ++i) {
+      const float y = __uint_as_float(__float_as_uint(x) + 1u);
+      if (!ok(y)) {
+        *out = x;
+        return true;
+      }
+      x = y;
+    }
+  } else {
+    for (int i = 0; i < 64 && x < -0x1p-100f; ++i) {
+      x = __uint_as_float(__float_as_uint(x) - 1u);
+      if (ok(x)) {
+        *out = x;
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+// The same from the logarithm: exp(x) of a float x != 0 is irrational, never a
+// midpoint between two floats, so exp_cr(x) >= w exactly when x > L = ln(the
+// midpoint of w and the float below it), and exp_cr(x) > w when x > ln(the
+// midpoint of w and the float above it). The smallest float above L is the
+// double logarithm rounded up when that lies clear of both neighbouring float
+// boundaries by more than its error (1 ulp documented; 4 allowed); otherwise the
+// stepping search decides. w is a positive normal float below 1.
+__device__ __forceinline__ bool nc_exp_threshold_log(float w, bool gt, float* out, int* slow_flag) {
+  const uint32_t wb = __float_as_uint(w);
+  const float nb = __uint_as_float(gt ? wb + 1u : wb - 1u);
+  const double L = log(0.5 * ((double)w + (double)nb));  // the midpoint is exact in double
+  float f = __double2float_ru(L);                          // smallest float >= L (L < 0)
+  if ((double)f == L) f = __uint_as_float(__float_as_uint(f) - 1u);
+  const float fp = __uint_as_float(__float_as_uint(f) + 1u);  // the float below f
+  const double err = fabs(L) * 0x1p-50;
+  if ((double)f - L > err && L - (double)fp > err) {
+    *out = f;
+    return true;
+  }
+  return nc_exp_threshold(w, gt, f, out, slow_flag);
+}
+
 // First index in [lo, hi) with a[i] >= t (hi when none).
 __device__ __forceinline__ int nc_first_ge(const float* a, int lo, int hi, float t) {
   while (lo < hi) {
@@ -334,15 +450,17 @@ __device__ __forceinline__ int nc_first_ge(const float* a, int lo, int hi, float
 }
 
 template <bool kCounts>
-__global__ void __launch_bounds__(NC_THREADS, 1)
+__global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
     nucleus_kernel(const __grid_constant__ SampleArgs a, FvScratch f, int K) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float s_fred[2][NC_WARPS];
-  __shared__ uint32_t s_u32[NC_WARPS + 1];
-  __shared__ double s_dbl[NC_WARPS + 1];
+  __shared__ uint32_t s_u32[33];
+  __shared__ double s_dbl[33];
   __shared__ int s_hn, s_nf, s_fail, s_slow, s_last, s_bK, s_cutn, s_nsp, s_again, s_done;
   __shared__ uint32_t s_qend;
-  __shared__ int s_nq;
+  __shared__ int s_ntie;
+  __shared__ uint16_t s_tlist[NC_TIES];
+  __shared__ uint32_t s_tna[NC_TIES];  // weights above the half point in that bucket
   __shared__ float s_vmax, s_vmin, s_total;
   // target state (thread 0): cutoff bucket / index, retained, sample, drawn bucket / index
   __shared__ int s_bc, s_ic, s_bs, s_is;
@@ -366,8 +484,9 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
     s_last = 0;
     s_bK = -1;
   }
-  for (int i = tid; i < NC_NB; i += NC_THREADS) s.cur[i] = 0u;
+  for (int i = tid; i <= NC_NB; i += NC_THREADS) s.cur[i] = 0u;
   if (tid < NC_NB / 32) s.tie[tid] = 0u;
+  if (tid == 0) s.bk[NC_NB] = 0;
   __syncthreads();
   if (!hist_ok) {
     if (tid == 0) {
@@ -398,8 +517,8 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
     }
     __syncthreads();
     if (warp == 0) {
-      mx = s_fred[0][lane];
-      mn = s_fred[1][lane];
+      mx = lane < NC_WARPS ? s_fred[0][lane] : -INFINITY;
+      mn = lane < NC_WARPS ? s_fred[1][lane] : INFINITY;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -430,10 +549,19 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   };
 
   // ---- 2. histogram -------------------------------------------------------------
-  nc_stream(lrow, V, P, scale, [&](float v, int) {
+  auto bin_rel = [&](float v) {  // bucket of a value, NC_NB when it never matters
     const float x = __fsub_rn(v, vmax);
-    if (x >= FV_XMIN) atomicAdd(&s.cur[bin(x)], 1u);
-  });
+    return x >= FV_XMIN ? bin(x) : NC_NB;
+  };
+  nc_stream4(
+      lrow, V, P, scale, [&](float v, int) { atomicAdd(&s.cur[bin_rel(v)], 1u); },
+      [&](float v0, float v1, float v2, float v3, int) {
+        const int b0 = bin_rel(v0), b1 = bin_rel(v1), b2 = bin_rel(v2), b3 = bin_rel(v3);
+        atomicAdd(&s.cur[b0], 1u);
+        atomicAdd(&s.cur[b1], 1u);
+        atomicAdd(&s.cur[b2], 1u);
+        atomicAdd(&s.cur[b3], 1u);
+      });
   __syncthreads();
   uint32_t cnt[NC_PER];
   int nrel;
@@ -515,9 +643,28 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
           const double sc = ldexp(1.0, 23 - el);
           const double tlo = wlo[j] * (1.0 - 0x1p-20) * sc, thi = whi[j] * (1.0 + 0x1p-20) * sc;
           const double hq = floor(tlo + 0.5);
+          float xl, xh;
           if (tlo > hq - 0.5 && thi < hq + 0.5 && (double)cnt[j] * hq < (double)NC_QMAX) {
             code |= NC_UNIFORM;
             q = cnt[j] * (uint32_t)hq;
+          } else if (tlo > hq - 0.5 && thi < hq + 1.5 &&
+                     (double)cnt[j] * (hq + 1.0) < (double)NC_QMAX) {
+            // one half point w_h = (hq + 1/2) grid: a weight rounds to hq units
+            // below it, hq + 1 above, and depends on the parity exactly at it;
+            // x thresholds of the correctly rounded exp decide which
+            const float wh = (float)((hq + 0.5) / sc);  // (2 hq + 1) 2^(e-24): exact
+            if (nc_exp_threshold_log(wh, false, &xl, &s_slow) &&
+                nc_exp_threshold_log(wh, true, &xh, &s_slow)) {
+              code |= NC_STRADDLE;
+              q = cnt[j] * (uint32_t)hq;
+              s.kq[b] = (uint32_t)hq;
+              s.send[b] = xl;  // weights at the half point from here
+              s.regS[b] = xh;  // weights above it from here
+            } else {
+              code = NC_SPECIAL;
+            }
+          } else {
+            code |= NC_MULTI;
           }
         }
       }
@@ -547,7 +694,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
     if (lane == 0) s_dbl[warp] = rmax;
     __syncthreads();
     if (warp == 0) {
-      double r = s_dbl[lane];
+      double r = lane < NC_WARPS ? s_dbl[lane] : 0.0;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) r = fmax(r, __shfl_xor_sync(0xffffffffu, r, o));
       if (lane == 0) s_dbl[32] = r;
@@ -575,78 +722,115 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   }
   __syncthreads();
 
-  // ---- 4. grid units of normal buckets; gather special ones ----------------------
-  // the weights the estimate cannot decide are queued in the (not yet used)
-  // bucket-end sums
-  float* exq = s.send;
-  if (tid == 0) s_nq = 0;
+  // ---- 4. pass: keys of special and predicted buckets; straddling buckets count ----
+  // the weights above their half point and note the ones exactly at it
+  if (tid == 0) s_ntie = 0;
   __syncthreads();
-  nc_stream(lrow, V, P, scale, [&](float v, int c) {
-    const float x = __fsub_rn(v, vmax);
-    if (!(x >= FV_XMIN)) return;
-    const int b = bin(x);
-    const uint32_t code = s.bk[b];
-    if (code & (NC_EXCL | NC_UNIFORM | NC_SPECIAL)) {
-      if (code & (NC_SPECIAL | NC_GATHER)) comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
-      return;
-    }
-    if (code & NC_GATHER) comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
-    const float sc = __int_as_float((127 + 23 - (int)(code & NC_EMASK)) << 23);  // 1 / grid
-    const float wa = __expf(x);
-    const float t = __fmul_rn(wa, sc);
-    const float fl = floorf(t);
-    const float fr = __fsub_rn(t, fl);
-    // 64 ulps of wa, in grid units
-    const float r = __fmul_rn(__uint_as_float((__float_as_uint(wa) & 0x7F800000u) - (17u << 23)), sc);
-    uint32_t q;
-    if (fabsf(__fsub_rn(fr, 0.5f)) > r) {
-      q = (uint32_t)fl + (fr > 0.5f ? 1u : 0u);
-    } else {
-      // too close to a half grid point for the estimate: decided after the pass
-      // by the correctly rounded exp, with the warps no longer diverging
-      const int qi = atomicAdd(&s_nq, 1);
-      if (qi < NC_QCAP) {
-        exq[qi] = x;
-        return;
-      }
-      if (!nc_units_exact(x, sc, &q, &s_slow)) {
-        atomicOr(&s.tie[b >> 5], 1u << (b & 31));
-        return;
-      }
-    }
-    if (q != 0u && atomicAdd(&s.qs[b], q) + q >= NC_QMAX) s_fail = 1;
-  });
-  __syncthreads();
-  for (int i = tid; i < min(s_nq, NC_QCAP); i += NC_THREADS) {
-    const float x = exq[i];
-    const int b = bin(x);
-    const float sc = __int_as_float((127 + 23 - (int)(s.bk[b] & NC_EMASK)) << 23);
-    uint32_t q;
-    if (!nc_units_exact(x, sc, &q, &s_slow)) atomicOr(&s.tie[b >> 5], 1u << (b & 31));
-    else if (q != 0u && atomicAdd(&s.qs[b], q) + q >= NC_QMAX) s_fail = 1;
-  }
-  __syncthreads();
-  // buckets with an exact half become special; one more pass gathers those
-  // that the last one did not
-  if (tid == 0) s_again = 0;
-  __syncthreads();
-  for (int b = tid; b < NC_NB; b += NC_THREADS) {
-    if ((s.tie[b >> 5] >> (b & 31)) & 1u) {
-      if (s.bk[b] & NC_GATHER) atomicAnd(&s.tie[b >> 5], ~(1u << (b & 31)));  // already gathered
-      else s_again = 1;
-      s.bk[b] = (uint16_t)NC_SPECIAL;
-    }
-  }
-  __syncthreads();
-  if (s_again) {
-    nc_stream(lrow, V, P, scale, [&](float v, int c) {
+  // one value with its bucket and the bucket's code (NC_NB: code 0, nothing to do)
+  auto p3_one = [&](float v, int c, int b, uint32_t code) {
+    if (code & (NC_SPECIAL | NC_GATHER | NC_MULTI)) comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
+    if (code & NC_STRADDLE) {
       const float x = __fsub_rn(v, vmax);
-      if (!(x >= FV_XMIN)) return;
-      const int b = bin(x);
-      if ((s.tie[b >> 5] >> (b & 31)) & 1u) comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
-    });
+      if (x >= s.regS[b]) {
+        atomicAdd(&s.qs[b], 1u);
+      } else if (x >= s.send[b]) {
+        const int i = atomicAdd(&s_ntie, 1);
+        if (i < NC_TIES) s_tlist[i] = (uint16_t)b;
+      }
+    }
+  };
+  nc_stream4(
+      lrow, V, P, scale,
+      [&](float v, int c) {
+        const int b = bin_rel(v);
+        p3_one(v, c, b, s.bk[b]);
+      },
+      [&](float v0, float v1, float v2, float v3, int c) {
+        const int b0 = bin_rel(v0), b1 = bin_rel(v1), b2 = bin_rel(v2), b3 = bin_rel(v3);
+        const uint32_t k0 = s.bk[b0], k1 = s.bk[b1], k2 = s.bk[b2], k3 = s.bk[b3];
+        constexpr uint32_t kAny = NC_SPECIAL | NC_GATHER | NC_MULTI | NC_STRADDLE;
+        if ((k0 | k1 | k2 | k3) & kAny) {
+          p3_one(v0, c, b0, k0);
+          p3_one(v1, c + 1, b1, k1);
+          p3_one(v2, c + 2, b2, k2);
+          p3_one(v3, c + 3, b3, k3);
+        }
+      });
+  __syncthreads();
+  if (s_ntie > NC_TIES) {
+    if (tid == 0) a.s.fixup[row] = 1u;
+    return;
+  }
+  // straddling buckets with weights at the half point are resolved in the walk
+  // from the parity of the sum before them: keep their count above it
+  if (tid < s_ntie) {
+    const int b = s_tlist[tid];
+    atomicOr(&s.tie[b >> 5], 1u << (b & 31));
+    s_tna[tid] = s.qs[b] - (s.pos[b + 1] - s.pos[b]) * s.kq[b];
+  }
+  __syncthreads();
+  for (int b = tid; b < NC_NB; b += NC_THREADS)
+    if ((s.tie[b >> 5] >> (b & 31)) & 1u) s.bk[b] = (uint16_t)(s.bk[b] | NC_TIEF);
+  __syncthreads();
+
+  // ---- 4b. grid units of multi buckets, one element per thread (gathered keys) ------
+  {
+    uint32_t nm[NC_PER], sum = 0u;
+    uint32_t ism = 0u;
+#pragma unroll
+    for (int j = 0; j < NC_PER; ++j) {
+      const int b = tid * NC_PER + j;
+      const bool m = (s.bk[b] & NC_MULTI) && s.pos[b + 1] > s.pos[b];
+      nm[j] = m ? s.pos[b + 1] - s.pos[b] : 0u;
+      ism += m ? 1u : 0u;
+      sum += nm[j];
+    }
+    uint32_t tot, ntot;
+    uint32_t off = nc_block_scan<uint32_t>(sum, s_u32, &tot);
+    uint32_t li = nc_block_scan<uint32_t>(ism, s_u32, &ntot);
+#pragma unroll
+    for (int j = 0; j < NC_PER; ++j) {
+      const int b = tid * NC_PER + j;
+      if (nm[j]) {
+        s.kq[b] = off;  // first flat index of the bucket
+        s.splist[li++] = (uint16_t)b;
+        off += nm[j];
+      }
+    }
+    if (tid < NC_NB / 32) s.gat[tid] = 0u;
+    __syncthreads();
+    for (uint32_t i = tid; i < tot; i += NC_THREADS) {
+      // the multi bucket holding flat index i: the last with kq <= i
+      int lo = 0, hi = (int)ntot - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s.kq[s.splist[mid]] <= i) lo = mid; else hi = mid - 1;
+      }
+      const int b = s.splist[lo];
+      const float x = __fsub_rn(fv_val(comp[s.pos[b] + (i - s.kq[b])]), vmax);
+      const float sc = __int_as_float((127 + 23 - (int)(s.bk[b] & NC_EMASK)) << 23);  // 1 / grid
+      const float wa = __expf(x);
+      const float t = __fmul_rn(wa, sc);
+      const float fl = floorf(t);
+      const float fr = __fsub_rn(t, fl);
+      // 64 ulps of wa, in grid units, bound the distance to the correctly rounded weight
+      const float r =
+          __fmul_rn(__uint_as_float((__float_as_uint(wa) & 0x7F800000u) - (17u << 23)), sc);
+      uint32_t q;
+      bool ok = true;
+      if (fabsf(__fsub_rn(fr, 0.5f)) > r) q = (uint32_t)fl + (fr > 0.5f ? 1u : 0u);
+      else ok = nc_units_exact(x, sc, &q, &s_slow);
+      if (!ok) atomicOr(&s.gat[b >> 5], 1u << (b & 31));
+      else if (q != 0u && atomicAdd(&s.qs[b], q) + q >= NC_QMAX) s_fail = 1;
+    }
+    __syncthreads();
+    // a multi bucket holding an exact half is walked element by element (its keys
+    // are gathered already)
+    for (int b = tid; b < NC_NB; b += NC_THREADS)
+      if ((s.gat[b >> 5] >> (b & 31)) & 1u) s.bk[b] = (uint16_t)NC_SPECIAL;
     __syncthreads();
   }
+
 
   // ---- 5. sort special buckets, their weights; prefix of the grid units ----------
   {
@@ -655,10 +839,10 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       const int b = tid * NC_PER + j;
-      const bool sp = (s.bk[b] & NC_SPECIAL) && s.pos[b + 1] > s.pos[b];
+      const bool sp = ((s.bk[b] & NC_SPECIAL) && s.pos[b + 1] > s.pos[b]) || (s.bk[b] & NC_TIEF);
       isp[j] = sp ? 1u : 0u;
       nsp_local += isp[j];
-      if (s.bk[b] & (NC_SPECIAL | NC_EXCL)) s.qs[b] = 0u;
+      if (s.bk[b] & (NC_SPECIAL | NC_EXCL | NC_TIEF)) s.qs[b] = 0u;
       qsum += s.qs[b];
     }
     uint32_t nsp, qtot;
@@ -685,13 +869,13 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   for (int k = warp; k < nsp; k += NC_WARPS) {
     const int b = s.splist[k];
     const int n = (int)(s.pos[b + 1] - s.pos[b]);
-    if (n <= NC_SORT_WARP) nc_warp_sort_any(comp + s.pos[b], n);
+    if (n <= NC_SORT_WARP && !(s.bk[b] & NC_TIEF)) nc_warp_sort_any(comp + s.pos[b], n);
   }
   __syncthreads();
   for (int k = 0; k < nsp; ++k) {
     const int b = s.splist[k];
     const int n = (int)(s.pos[b + 1] - s.pos[b]);
-    if (n > NC_SORT_WARP) {
+    if (n > NC_SORT_WARP && !(s.bk[b] & NC_TIEF)) {
       if (n > NC_SORT_BIG) {
         if (tid == 0) s_fail = 1;
         break;
@@ -719,6 +903,8 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   __syncthreads();
   const int cutn = s_cutn;
   auto n_eff = [&](int b) { return b == bK ? cutn : (int)(s.pos[b + 1] - s.pos[b]); };
+  // elements the walk takes one by one (none for a straddling bucket)
+  auto n_walk = [&](int b) { return (s.bk[b] & NC_TIEF) ? 0 : n_eff(b); };
   // the walk reads the special elements' weights from shared memory (the
   // cursor array, free until the cutoff search) when they fit, in splist order
   float* stage = reinterpret_cast<float*>(s.cur);
@@ -728,7 +914,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       const int k = tid * NC_PER + j;
-      ne[j] = k < nsp ? (uint32_t)n_eff(s.splist[k]) : 0u;
+      ne[j] = k < nsp ? (uint32_t)n_walk(s.splist[k]) : 0u;
       sum += ne[j];
     }
     uint32_t total;
@@ -747,7 +933,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
     bool slow = false;
     for (int k = warp; k < nsp; k += NC_WARPS) {
       const int b = s.splist[k];
-      const int p0 = (int)s.pos[b], n = n_eff(b);
+      const int p0 = (int)s.pos[b], n = n_walk(b);
       float* w = staged ? stage + s.soff[k] : ssum + p0;
       for (int i = lane; i < n; i += 32) w[i] = exp_cr(__fsub_rn(fv_val(comp[p0 + i]), vmax), slow);
     }
@@ -778,8 +964,40 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
       if (lane == 0) s.regS[k] = S;
       region(b0);
       if (fail) break;
+      if (s.bk[b0] & NC_TIEF) {
+        // in sorted order: na weights above the half point (kq + 1 units
+        // each), the nt at it (kq units plus one when that makes the sum's
+        // last mantissa bit even), the rest below (kq units)
+        const uint32_t sb = __float_as_uint(S);
+        const int e = (int)((sb >> 23) & 0xFFu) - 127;
+        if (S == 0.0f || e != (int)(s.bk[b0] & NC_EMASK)) {
+          fail = true;
+          break;
+        }
+        const uint64_t kq = s.kq[b0], cntb = s.pos[b0 + 1] - s.pos[b0];
+        uint64_t nt = 0, na = 0;
+        for (int i = 0; i < s_ntie; ++i)
+          if (s_tlist[i] == b0) {
+            ++nt;
+            na = s_tna[i];
+          }
+        uint64_t M = ((sb & 0x7FFFFFu) | 0x800000u) + na * (kq + 1u);
+        for (uint64_t t = 0; t < nt && M < (1u << 24); ++t) M += kq + ((M + kq) & 1u);
+        M += (cntb - na - nt) * kq;
+        if (na + nt > cntb || M >= (1u << 24)) {
+          fail = true;
+          break;
+        }
+        S = __uint_as_float((sb & 0xFF800000u) | ((uint32_t)M & 0x7FFFFFu));
+        if (lane == 0) s.send[b0] = S;
+        prev = b0 + 1;
+        k = k + 1;
+        continue;
+      }
       int k2 = k;
-      while (k2 + 1 < nsp && s.splist[k2 + 1] == s.splist[k2] + 1) ++k2;
+      while (k2 + 1 < nsp && s.splist[k2 + 1] == s.splist[k2] + 1 &&
+             !(s.bk[s.splist[k2 + 1]] & NC_TIEF))
+        ++k2;
       const int bl = s.splist[k2];
       const int p0 = (int)s.pos[b0];
       const int len = (int)s.pos[bl] + n_eff(bl) - p0;
@@ -806,7 +1024,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   if (staged) {  // the element sums of special buckets, for the cutoff search
     for (int k = warp; k < nsp; k += NC_WARPS) {
       const int b = s.splist[k];
-      const int p0 = (int)s.pos[b], n = n_eff(b);
+      const int p0 = (int)s.pos[b], n = n_walk(b);
       for (int i = lane; i < n; i += 32) ssum[p0 + i] = stage[s.soff[k] + i];
     }
     __syncthreads();
@@ -818,6 +1036,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
 
   // ---- 6. sums at the ends of normal buckets, each checked -------------------------
   for (int b = tid; b <= last; b += NC_THREADS) {
+    if (s.bk[b] & NC_TIEF) continue;  // set by the walk
     if (s.bk[b] & NC_SPECIAL) {
       if (s.pos[b + 1] == s.pos[b]) s.send[b] = 0.0f;  // empty special: filled below
       continue;
@@ -904,7 +1123,7 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
   auto request = [&](int b) {
     s.gat[b >> 5] |= 1u << (b & 31);
     s_again = 1;
-    if (!(s.bk[b] & NC_GATHER)) s_pass = 1;
+    if (!(s.bk[b] & (NC_GATHER | NC_MULTI))) s_pass = 1;
   };
   if (tid < NC_NB / 32) s.gat[tid] = 0u;
   if (tid == 0) {
@@ -963,13 +1182,13 @@ __global__ void __launch_bounds__(NC_THREADS, 1)
     // sum them from their exact start
     if (s_pass) {
       for (int b = tid; b <= last; b += NC_THREADS)
-        if (marked(b) && !(s.bk[b] & NC_GATHER)) s.cur[b] = s.pos[b];
+        if (marked(b) && !(s.bk[b] & (NC_GATHER | NC_MULTI))) s.cur[b] = s.pos[b];
       __syncthreads();
       nc_stream(lrow, V, P, scale, [&](float v, int c) {
         const float x = __fsub_rn(v, vmax);
         if (!(x >= FV_XMIN)) return;
         const int b = bin(x);
-        if (b <= last && marked(b) && !(s.bk[b] & NC_GATHER))
+        if (b <= last && marked(b) && !(s.bk[b] & (NC_GATHER | NC_MULTI)))
           comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
       });
       __syncthreads();

@@ -134,3 +134,36 @@ def test_nonfinite_rows_are_flagged(gpu_sampler, oracle):
               uniforms=np.array([0.5, 0.5, 0.5], np.float32),
               params=dict(temperature=1.0, top_p=0.9, top_k=native.INT_MAX))
     check(gpu_sampler, oracle, wl, "non-finite rows")
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_randomized_sweep(gpu_sampler, oracle, seed):
+    # random row shapes, value distributions (normal, heavy-tailed, quantised,
+    # Zipf-ranked), temperatures, top-p, large top-k and all three penalties
+    rng = np.random.default_rng(1000 + seed)
+    B = 16
+    V = int(rng.choice([1000, 4099, 32000, 50257, 128256, 151936]))
+    kind = seed % 4
+    if kind == 0:
+        logits = rng.standard_normal((B, V)).astype(np.float32) * np.float32(rng.uniform(0.05, 8.0))
+    elif kind == 1:
+        logits = rng.standard_t(2.5, (B, V)).astype(np.float32) * np.float32(rng.uniform(0.3, 3.0))
+    elif kind == 2:
+        lg = rng.standard_normal((B, V)).astype(np.float32) * np.float32(2.0)
+        m, e = np.frexp(lg)
+        q = np.float32(2.0 ** int(rng.integers(5, 11)))
+        logits = np.ldexp(np.round(m * q) / q, e).astype(np.float32)
+    else:
+        wl = workloads.zipf_ranked(B=B, V=V, H=64, seed=seed)
+        logits = wl["logits"]
+    H = int(rng.integers(0, 600))
+    hist = rng.integers(0, V, B * H).astype(np.int32)
+    offs = (np.arange(B + 1) * H).astype(np.int32)
+    top_k = native.INT_MAX if rng.random() < 0.7 else int(rng.integers(1100, max(1101, V)))
+    params = dict(temperature=float(rng.uniform(0.3, 2.0)), top_p=float(rng.choice([rng.uniform(0.05, 0.999), 1.0])),
+                  top_k=top_k, repetition_penalty=float(rng.uniform(0.8, 1.6)),
+                  frequency_penalty=float(rng.choice([0.0, rng.uniform(-0.2, 0.8)])),
+                  presence_penalty=float(rng.choice([0.0, rng.uniform(-0.2, 0.8)])))
+    wl = dict(logits=np.ascontiguousarray(logits), hist_ids=hist, hist_offsets=offs,
+              uniforms=rng.random(B).astype(np.float32), params=params)
+    check(gpu_sampler, oracle, wl, f"sweep seed={seed} V={V} kind={kind} {params}", max_full_sort=2)
