@@ -567,6 +567,9 @@ __global__ void __launch_bounds__(FV_THREADS, 1) fullvocab_fixup_kernel(const __
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_list[FV_FIXUP_MAX_LIST];
   __shared__ int s_n;
+  // the next launch on the stream may be scheduled now; it waits for this
+  // grid's completion before it reads anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // launched as a programmatic dependent of the top-k kernel: it may start
   // while that kernel drains, and waits here until its writes are visible
   asm volatile("griddepcontrol.wait;" ::: "memory");

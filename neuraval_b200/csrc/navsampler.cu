@@ -387,10 +387,21 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     a.bm_words = (a.seg_len + 31) / 32 + 1;
     const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
     if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
-    dim3 grid(S, rows);
-    if (counts) nvs::topk_ldg_kernel<true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
-    else nvs::topk_ldg_kernel<false><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    // a programmatic dependent launch: scheduled while the previous kernel on
+    // the stream finishes; the kernel waits for it before its first read
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(S, rows);
+    cfg.blockDim = dim3(nvs::TL_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = counts ? cudaLaunchKernelEx(&cfg, nvs::topk_ldg_kernel<true, false>, a)
+                                 : cudaLaunchKernelEx(&cfg, nvs::topk_ldg_kernel<false, false>, a);
+    if (e != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
     // rows whose ties overflowed the candidate buffers (normally none)
     return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, true, 8);
   }

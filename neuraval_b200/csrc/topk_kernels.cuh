@@ -69,12 +69,14 @@ struct SampleArgs {
   PxArgs px;            // peers of a shard kernel (px.shards == 0: none)
 };
 
-// Shared penalty state for the CTA's column range [c0,c1). Returns false when
-// the row's in-range history does not fit h_cap (BAD_HISTORY).
+constexpr int HIST_PRE = 4;  // history ids per thread loaded before any is used
+
+// Shared penalty state for the CTA's column range [c0,c1), from the row's
+// history ids [hb, he). Returns false when the row's in-range history does
+// not fit h_cap (BAD_HISTORY).
 template <bool kCounts>
-__device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, int c1,
-                              uint32_t* bitmap, int32_t* hsorted, int* s_hn) {
-  const int hb = a.hoff[row], he = a.hoff[row + 1];
+__device__ bool setup_penalty_range(Penalty& P, const SampleArgs& a, int hb, int he, int c0,
+                                    int c1, uint32_t* bitmap, int32_t* hsorted, int* s_hn) {
   const int H = he - hb;
   P.bitmap = bitmap;
   P.hsorted = hsorted;
@@ -92,12 +94,19 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
   // frequency (either sign) cnt * f is that zero for every count, so the ids
   // are neither collected nor sorted (P.hn stays 0, every count reads 0)
   const bool counting = kCounts && P.cnt && P.freq != 0.0f;
+  // the thread's first ids are all in flight before any is used (one round
+  // trip, hidden behind the bitmap clear)
+  int pre[HIST_PRE];
+#pragma unroll
+  for (int k = 0; k < HIST_PRE; ++k) {
+    const int h = hb + (int)threadIdx.x + k * (int)blockDim.x;
+    pre[k] = h < he ? a.hist[h] : 0;
+  }
   const int words = ((c1 - c0 + 31) >> 5) + 1;  // one spare word for 4-id windows
   for (int i = threadIdx.x; i < words; i += blockDim.x) bitmap[i] = 0u;
   if (threadIdx.x == 0) *s_hn = 0;
   __syncthreads();
-  for (int h = hb + threadIdx.x; h < he; h += blockDim.x) {
-    const int id = a.hist[h];
+  auto put = [&](int id) {
     if (id >= c0 && id < c1) {
       const int rel = id - c0;
       atomicOr(&bitmap[rel >> 5], 1u << (rel & 31));
@@ -106,7 +115,12 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
         if (slot < a.h_cap) hsorted[slot] = id;
       }
     }
-  }
+  };
+#pragma unroll
+  for (int k = 0; k < HIST_PRE; ++k)
+    if (hb + (int)threadIdx.x + k * (int)blockDim.x < he) put(pre[k]);
+  for (int h = hb + (int)threadIdx.x + HIST_PRE * (int)blockDim.x; h < he; h += blockDim.x)
+    put(a.hist[h]);
   __syncthreads();
   bool ok = true;
   if (counting) {
@@ -122,6 +136,13 @@ __device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, 
     }
   }
   return ok;
+}
+
+template <bool kCounts>
+__device__ bool setup_penalty(Penalty& P, const SampleArgs& a, int row, int c0, int c1,
+                              uint32_t* bitmap, int32_t* hsorted, int* s_hn) {
+  return setup_penalty_range<kCounts>(P, a, a.hoff[row], a.hoff[row + 1], c0, c1, bitmap,
+                                      hsorted, s_hn);
 }
 
 // ---------------------------------------------------------------------------

@@ -211,6 +211,11 @@ template <bool kCounts, bool kShard = false>
 __global__ void __launch_bounds__(TL_THREADS, 2)
     topk_ldg_kernel(const __grid_constant__ SampleArgs a) {
   __shared__ int s_owner;
+  // launched as a programmatic dependent of whatever precedes it on the stream
+  // (the producer of the logits, the previous call's fix-up): its launch
+  // overlaps that kernel's end, and nothing is read before that kernel's
+  // writes are visible (a no-op for an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   topk_ldg_body<kCounts, kShard>(a, &s_owner);
   if constexpr (kShard) {
     if (a.px.shards > 0) {
@@ -264,7 +269,9 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   const int n4 = (a1 - a0) >> 2;
   const float4* body = reinterpret_cast<const float4*>(lrow + a0);
 
-  // the sample's loads go out first; the penalty tables are built meanwhile
+  // the history offsets, then the sample's loads; the penalty tables are built
+  // while the sample is in flight
+  const int hb = a.hoff[row], he = a.hoff[row + 1];
   float4 x0[TL_UNROLL];
 #pragma unroll
   for (int u = 0; u < TL_UNROLL; ++u) {
@@ -275,7 +282,8 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   if (!kShard && tid == 0) s_u = a.uniforms[row];  // read by the finish
 
   Penalty P;
-  const bool hist_ok = setup_penalty<kCounts>(P, a, row, c0, c1, bitmap, hsorted, &s_hn);
+  const bool hist_ok =
+      setup_penalty_range<kCounts>(P, a, hb, he, c0, c1, bitmap, hsorted, &s_hn);
   if (tid == 0) {
     s_pen = P;
     s_nonfinite = 0;
@@ -422,6 +430,9 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
     __syncwarp();
     qn = 0;
   }
+  // the stream is done: the kernel that follows (the fix-up) may be scheduled
+  // once every CTA is here; it waits for this grid's completion before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (nonfinite) s_nonfinite = 1;
   if (tie_ovf && lane == 0) s_overflow = 1;
   // the final select's histogram range: [largest warp threshold, largest
