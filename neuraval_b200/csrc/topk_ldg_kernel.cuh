@@ -530,19 +530,38 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
     const uint32_t vk = (uint32_t)(key >> 32);
     int cnt = 0;
     if (key != 0ull && vk >= lb) {
+      // values of each list greater than vk (a sorted prefix): the eight
+      // searches are independent chains the scheduler interleaves; equal
+      // values, which rank by id, are rare and counted afterwards
+      constexpr int NL = TL_WARPS / 2;
+      int pos[NL];
 #pragma unroll
-      for (int t = 0; t < TL_WARPS / 2; ++t) {
-        const int l = half * (TL_WARPS / 2) + t;
-        if (l == warp) continue;  // within its own list a key's rank is its place j
-        const uint32_t* L = lval + l * TL_TOPW;
-        int pos = 0;  // values of list l greater than vk (a sorted prefix)
+      for (int t = 0; t < NL; ++t) {
+        const uint32_t* L = lval + (half * NL + t) * TL_TOPW;
+        int p = 0;
 #pragma unroll
         for (int step = TL_TOPW / 2; step > 0; step >>= 1)
-          if (L[pos + step - 1] > vk) pos += step;
-        pos += L[pos] > vk ? 1 : 0;
-        cnt += pos;
-        // equal values rank by id: count those with a larger full key
-        for (int q = pos; q < TL_TOPW && L[q] == vk; ++q) cnt += lists[l * TL_TOPW + q] > key;
+          if (L[p + step - 1] > vk) p += step;
+        p += L[p] > vk ? 1 : 0;
+        pos[t] = p;
+      }
+      unsigned eq = 0u;
+#pragma unroll
+      for (int t = 0; t < NL; ++t) {
+        const int l = half * NL + t;
+        if (l == warp) continue;  // within its own list a key's rank is its place j
+        cnt += pos[t];
+        if (pos[t] < TL_TOPW && lval[l * TL_TOPW + pos[t]] == vk) eq |= 1u << t;
+      }
+      if (eq != 0u) {
+#pragma unroll
+        for (int t = 0; t < NL; ++t) {
+          if (!(eq & (1u << t))) continue;
+          const int l = half * NL + t;
+          // equal values rank by id: count those with a larger full key
+          for (int q = pos[t]; q < TL_TOPW && lval[l * TL_TOPW + q] == vk; ++q)
+            cnt += lists[l * TL_TOPW + q] > key;
+        }
       }
     }
     cnt += __shfl_xor_sync(0xffffffffu, cnt, 16);
