@@ -40,7 +40,10 @@ constexpr int TL_UNROLL = 4;                       // float4 loads in flight per
 constexpr int TL_STEP = TL_THREADS * TL_UNROLL;    // float4 per CTA step
 constexpr int TL_KMAX = 64;
 constexpr int TL_WORK = 32768;                     // finish / merge / histogram / queue area
-constexpr int TL_QCAP = 256;                       // queued float4 indices per warp
+// Queued float4s per warp during the stream (value and index), in the
+// candidate-list and work areas (contiguous, 48 KiB, unused while streaming).
+constexpr int TL_QV = 152;
+static_assert(TL_WARPS * TL_QV * 20 <= TK_CAPB * 8 + TL_WORK, "stream queues do not fit");
 
 inline size_t tl_smem_bytes(int bm_words, int h_cap) {
   return (size_t)TL_WARPS * TW_WCAP * 8      // warp buffers
@@ -357,11 +360,14 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   }
 
   // ---- stream -----------------------------------------------------------------
-  // The loop only queues the index of every float4 that may hold a candidate
-  // (raw*scale >= theta, a superset when penalties only lower values), a NaN or
-  // +inf, or -- for penalties that can raise a value -- a penalised id. The
-  // queue is drained outside the loop: exact values, then warp appends.
-  int* queue = reinterpret_cast<int*>(work) + warp * TL_QCAP;
+  // The loop only queues every float4 that may hold a candidate (raw*scale >=
+  // theta, a superset when penalties only lower values), a NaN or +inf, or --
+  // for penalties that can raise a value -- a penalised id: its value and
+  // index, so the drain outside the loop reads nothing from global memory
+  // again (exact values, then warp appends).
+  float4* qval = reinterpret_cast<float4*>(cv) + warp * TL_QV;
+  int* qidx = reinterpret_cast<int*>(reinterpret_cast<float4*>(cv) + TL_WARPS * TL_QV) +
+              warp * TL_QV;
   const bool force_pen = pen_active && !pen_lowers;
   int qn = 0;
   int base = tid;
@@ -387,11 +393,15 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
         flag = flag && q < n4;
         const unsigned b = __ballot_sync(0xffffffffu, flag);
         if (b != 0u) {
-          if (flag) queue[qn + __popc(b & ((1u << lane) - 1u))] = q;
+          if (flag) {
+            const int at = qn + __popc(b & ((1u << lane) - 1u));
+            qval[at] = x[u];
+            qidx[at] = q;
+          }
           qn += __popc(b);
         }
       }
-      if (qn > TL_QCAP - 32 * TL_UNROLL) {
+      if (qn > TL_QV - 32 * TL_UNROLL) {
         base += TL_STEP;
         more = true;
         break;
@@ -399,18 +409,11 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
     }
     // drain: exact values of the queued float4s, appended to the warp buffer
     __syncwarp();
-    int qnext = lane < qn ? queue[lane] : 0;
-    float4 xnext = lane < qn ? __ldcg(body + qnext) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = 0; i0 < qn; i0 += 32) {
       const int i = i0 + lane;
       const bool valid = i < qn;
-      const int q = qnext;
-      const float4 x = xnext;
-      if (i0 + 32 < qn) {  // next batch of loads in flight while this one is processed
-        const bool vn = i + 32 < qn;
-        qnext = vn ? queue[i + 32] : 0;
-        xnext = vn ? __ldcg(body + qnext) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      const int q = valid ? qidx[i] : 0;
+      const float4 x = valid ? qval[i] : make_float4(0.f, 0.f, 0.f, 0.f);
       const int col = a0 + 4 * q;
       float e[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
@@ -430,6 +433,8 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
     __syncwarp();
     qn = 0;
   }
+  // every warp's queue is drained before the lists below reuse that area
+  __syncthreads();
   // the stream is done: the kernel that follows (the fix-up) may be scheduled
   // once every CTA is here; it waits for this grid's completion before reading
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
