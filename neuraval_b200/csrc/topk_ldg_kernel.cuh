@@ -6,7 +6,8 @@
 //    flight (evict-first), so the row is read once with no shared-memory
 //    staging and no barrier in the loop. Per value the loop does one multiply,
 //    one NaN/+inf test and one threshold test; one ballot per float4 queues
-//    the float4s that may hold a candidate for a drain outside the loop;
+//    the float4s that may hold a candidate (values and indices, in shared
+//    memory) for a drain outside the loop;
 //  - the first step is also the sample: exact (penalised) values, each
 //    thread's maximum, and a lower bound of the K-th largest of those 512
 //    maxima -- distinct elements of the segment, so a lower bound of its K-th
