@@ -139,6 +139,27 @@ static int choose_splits(int rows, int V, int num_sms, int forced) {
   return S;
 }
 
+// Column segments per row for the k <= 64 top-k kernel: every extra segment
+// of a row costs its own head and tail plus the merge of the row's segments
+// (about 12 us on a B200), against a stream of 4*V/S bytes at one CTA's rate
+// (about 26 GB/s). S minimises 12*[S > 1] + 4V / (S * 26e3) us over powers of
+// two up to 8 that keep the grid in one wave (rows * S <= 2 * SMs) and
+// segments of at least 8192 columns. NAVSAMPLER_SPLITS overrides.
+static int choose_splits_topk(int rows, int V, int num_sms, int forced) {
+  if (forced >= 1) return forced;
+  int best = 1;
+  double tbest = 4.0 * V / 26000.0;
+  for (int S = 2; S <= 8; S *= 2) {
+    if ((long long)rows * S > 2LL * num_sms || V / S < 8192) break;
+    const double t = 12.0 + 4.0 * V / (S * 26000.0);
+    if (t < tbest) {
+      tbest = t;
+      best = S;
+    }
+  }
+  return best;
+}
+
 // The dynamic shared memory limit of every kernel is raised once per handle
 // (a per-function attribute), not on every call.
 static bool raise_smem_limits(int limit) {
@@ -380,7 +401,7 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
 
   const int K = prm->top_k < V ? prm->top_k : V;
   if (K < V && K <= nvs::TL_KMAX) {
-    int S = choose_splits(rows, V, h->num_sms, h->forced_splits);
+    int S = choose_splits_topk(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);
     S = (V + a.seg_len - 1) / a.seg_len;
     if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
@@ -826,7 +847,8 @@ static int launch_shard_candidates(NcbSampler* h, const float* d_logits, int row
   a.shard_out = records;
   const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
   a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
-  int S = choose_splits(rows, width, h->num_sms, h->forced_splits);
+  int S = prm->greedy ? choose_splits(rows, width, h->num_sms, h->forced_splits)
+                      : choose_splits_topk(rows, width, h->num_sms, h->forced_splits);
   a.seg_len = round_up((width + S - 1) / S, 4);
   S = (width + a.seg_len - 1) / a.seg_len;
   if ((size_t)rows * S > (size_t)h->max_ctas) return NCB_ERROR_CAPACITY;
