@@ -833,10 +833,21 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   __threadfence();
   float* uv = reinterpret_cast<float*>(work);            // union: [0, 8 KiB)
   int* uid = reinterpret_cast<int*>(uv + TK_CAPB);        //        [8, 16 KiB)
+  // the segments' candidate counts, one thread per segment, then offsets
+  constexpr int MAX_SEG = 64;
+  __shared__ int s_segoff[MAX_SEG + 1];
+  const bool flat = S <= MAX_SEG;
+  if (flat && tid < S) s_segoff[tid + 1] = __ldcg(&a.s.cand_n[row * S + tid]);
+  if (tid == 0) s_state = __ldcg(&a.s.rowstate[row]);
+  __syncthreads();
   if (tid == 0) {
-    s_state = __ldcg(&a.s.rowstate[row]);
     int tot = 0;
-    for (int sp = 0; sp < S; ++sp) tot += __ldcg(&a.s.cand_n[row * S + sp]);
+    if (flat) {
+      s_segoff[0] = 0;
+      for (int sp = 0; sp < S; ++sp) s_segoff[sp + 1] = (tot += s_segoff[sp + 1]);
+    } else {
+      for (int sp = 0; sp < S; ++sp) tot += __ldcg(&a.s.cand_n[row * S + sp]);
+    }
     s_tot = tot;
   }
   __syncthreads();
@@ -846,15 +857,30 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
   int mm = 0;
   float mkth = -INFINITY;
   if (mstate == 0u) {
-    int off = 0;
-    for (int sp = 0; sp < S; ++sp) {
-      const int n = __ldcg(&a.s.cand_n[row * S + sp]);
-      const size_t g = (size_t)(row * S + sp) * TK_CAPB;
-      for (int i = tid; i < n; i += TL_THREADS) {
-        uv[off + i] = __ldcg(&a.s.cand_v[g + i]);
-        uid[off + i] = __ldcg(&a.s.cand_id[g + i]);
+    if (flat) {
+      // every segment's candidates in one flat pass (loads in flight together)
+      for (int j = tid; j < total; j += TL_THREADS) {
+        int lo = 0, hi = S - 1;  // the segment sp with s_segoff[sp] <= j < s_segoff[sp + 1]
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_segoff[mid] <= j) lo = mid;
+          else hi = mid - 1;
+        }
+        const size_t g = (size_t)(row * S + lo) * TK_CAPB + (j - s_segoff[lo]);
+        uv[j] = __ldcg(&a.s.cand_v[g]);
+        uid[j] = __ldcg(&a.s.cand_id[g]);
       }
-      off += n;
+    } else {
+      int off = 0;
+      for (int sp = 0; sp < S; ++sp) {
+        const int n = __ldcg(&a.s.cand_n[row * S + sp]);
+        const size_t g = (size_t)(row * S + sp) * TK_CAPB;
+        for (int i = tid; i < n; i += TL_THREADS) {
+          uv[off + i] = __ldcg(&a.s.cand_v[g + i]);
+          uid[off + i] = __ldcg(&a.s.cand_id[g + i]);
+        }
+        off += n;
+      }
     }
     __syncthreads();
     if (total <= RS_MAX) {

@@ -75,8 +75,8 @@ __device__ void merge_row(const MergeArgs& g) {
   int* cid = reinterpret_cast<int*>(cv + TK_CAPB);                       // [CAPB]
   unsigned char* work = reinterpret_cast<unsigned char*>(cid + TK_CAPB);  // VM_WORK
   uint32_t* hist = reinterpret_cast<uint32_t*>(work + VM_WORK);          // [256]
-  __shared__ int s_n[VM_MAX_SHARDS], s_off[VM_MAX_SHARDS + 1];
-  __shared__ uint32_t s_state, s_kth[VM_MAX_SHARDS];
+  __shared__ int s_n[VM_MAX_SHARDS], s_off[VM_MAX_SHARDS + 1], s_cnt[VM_MAX_SHARDS];
+  __shared__ uint32_t s_state, s_kth[VM_MAX_SHARDS], s_rst[VM_MAX_SHARDS];
   __shared__ int s_sh[2], s_count, s_ovf, s_nu;
   __shared__ float s_lb;
 
@@ -86,22 +86,34 @@ __device__ void merge_row(const MergeArgs& g) {
   const size_t stride = (size_t)g.rows * VS_REC_WORDS;
   const uint32_t* rec0 = g.recs + (size_t)row * VS_REC_WORDS;
 
+  // every shard's header at once (one thread per shard), then the offsets
+  if (tid < G) {
+    const uint32_t* r = rec0 + tid * stride;
+    const uint32_t h0 = r[0], h1 = r[1], h2 = r[2], h3 = r[3];
+    s_n[tid] = min((int)h0, VS_CAP);
+    s_rst[tid] = h1;
+    s_kth[tid] = h2;
+    s_cnt[tid] = (int)h3;
+  }
+  __syncthreads();
   if (tid == 0) {
     uint32_t st = 0u;
     int off = 0;
     for (int s = 0; s < G; ++s) {
-      const uint32_t* r = rec0 + s * stride;
-      const int n = min((int)r[0], VS_CAP);
-      s_n[s] = n;
       s_off[s] = off;
-      s_kth[s] = r[2];
-      off += n;
-      st |= r[1];
+      off += s_n[s];
+      st |= s_rst[s];
     }
     s_off[G] = off;
     s_state = st;
   }
   __syncthreads();
+  // the shard holding union entry j (entries in shard order)
+  auto shard_of = [&](int j) {
+    int s = 0;
+    while (s + 1 < G && s_off[s + 1] <= j) ++s;
+    return s;
+  };
   const uint32_t st = s_state;
   const int total = s_off[G];
 
@@ -148,25 +160,26 @@ __device__ void merge_row(const MergeArgs& g) {
     // shard that holds K values (a lower bound of the global K-th value).
     if (tid == 0) {
       float lb = -INFINITY;
-      for (int s = 0; s < G; ++s) {
-        const uint32_t* r = rec0 + s * stride;
-        if ((int)r[3] >= K) lb = fmaxf(lb, __uint_as_float(r[2]));
-      }
+      for (int s = 0; s < G; ++s)
+        if (s_cnt[s] >= K) lb = fmaxf(lb, __uint_as_float(s_kth[s]));
       s_lb = lb;
       s_nu = 0;
     }
     __syncthreads();
     const float lb = s_lb;
-    for (int s = 0; s < G; ++s) {
+    // all shards' entries in one flat pass: every thread's loads are in flight
+    // together instead of one shard after another
+    for (int j = tid; j < total; j += VM_THREADS) {
+      const int s = shard_of(j);
       const uint32_t* r = rec0 + s * stride;
-      for (int i = tid; i < s_n[s]; i += VM_THREADS) {
-        const float v = __uint_as_float(r[VS_HDR + i]);
-        if (v >= lb) {
-          const int slot = atomicAdd(&s_nu, 1);
-          if (slot < RS_MAX) {
-            uv[slot] = v;
-            uid[slot] = (int)r[VS_HDR + VS_CAP + i];
-          }
+      const int i = j - s_off[s];
+      const float v = __uint_as_float(r[VS_HDR + i]);
+      const int id = (int)r[VS_HDR + VS_CAP + i];
+      if (v >= lb) {
+        const int slot = atomicAdd(&s_nu, 1);
+        if (slot < RS_MAX) {
+          uv[slot] = v;
+          uid[slot] = id;
         }
       }
     }
@@ -181,10 +194,9 @@ __device__ void merge_row(const MergeArgs& g) {
         if (tid == 0) {
           bool cut = false;
           if (st & VS_OVF_AT_KTH)
-            for (int s = 0; s < G; ++s) {
-              const uint32_t rs_ = rec0[s * stride + 1];
-              if ((rs_ & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == cand_val(rs.x)) cut = true;
-            }
+            for (int s = 0; s < G; ++s)
+              if ((s_rst[s] & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == cand_val(rs.x))
+                cut = true;
           s_ovf = cut ? 1 : 0;
         }
         __syncthreads();
@@ -205,13 +217,12 @@ __device__ void merge_row(const MergeArgs& g) {
     }
     __syncthreads();
   }
-  for (int s = 0; s < G; ++s) {
+  for (int j = tid; j < total; j += VM_THREADS) {
+    const int s = shard_of(j);
     const uint32_t* r = rec0 + s * stride;
-    const int n = s_n[s], o = s_off[s];
-    for (int i = tid; i < n; i += VM_THREADS) {
-      uv[o + i] = __uint_as_float(r[VS_HDR + i]);
-      uid[o + i] = (int)r[VS_HDR + VS_CAP + i];
-    }
+    const int i = j - s_off[s];
+    uv[j] = __uint_as_float(r[VS_HDR + i]);
+    uid[j] = (int)r[VS_HDR + VS_CAP + i];
   }
   __syncthreads();
   // fewer than K finite values in the whole row: every finite value is a
@@ -223,10 +234,8 @@ __device__ void merge_row(const MergeArgs& g) {
     // the global K-th value
     bool cut = false;
     if (st & VS_OVF_AT_KTH)
-      for (int s = 0; s < G; ++s) {
-        const uint32_t rs = rec0[s * stride + 1];
-        if ((rs & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == theta) cut = true;
-      }
+      for (int s = 0; s < G; ++s)
+        if ((s_rst[s] & VS_OVF_AT_KTH) && __uint_as_float(s_kth[s]) == theta) cut = true;
     s_ovf = cut ? 1 : 0;
     s_count = 0;
   }
