@@ -226,65 +226,67 @@ __device__ __noinline__ void finish_keys_warp(const SampleArgs& a, int row, uint
 }
 
 // The rest of the finish once the weights w[i] = exp(v_i - max) of the m
-// sorted candidates are in shared memory (`S`: 64 floats of scratch).
+// sorted candidates are in shared memory (`S`: 64 floats of scratch, unused).
+// Every lane runs the same sequential fp32 sums (TokenSampler.cs:96-103) on
+// weights broadcast from registers and keeps S[lane] and S[lane + 32], so the
+// cutoff (:105-119) and draw (:125-132) searches are ballots on registers; the
+// boundary tests run on four lanes at once.
 __device__ __noinline__ void finish_weights_warp(const SampleArgs& a, int row, uint64_t k0,
                                                 uint64_t k1, int m, const float* __restrict__ w,
                                                 float* __restrict__ S, bool any_slow, float u) {
+  (void)S;
   const int lane = threadIdx.x & 31;
   uint64_t k[2] = {k0, k1};
-  // sequential fp32 sums in sorted order (lane 0; w and S do not overlap, so
-  // the loads run ahead of the dependent adds), then the cutoff and draw
-  // searches by ballot
-  if (lane == 0) {
-    float total = 0.0f;
-    int i = 0;
-    for (; i + 8 <= m; i += 8) {
-      float t[8];
+  const float w_lo = lane < m ? w[lane] : 0.0f;
+  const float w_hi = lane + 32 < m ? w[lane + 32] : 0.0f;
+  float s_lo = 0.0f, s_hi = 0.0f, total = 0.0f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) t[q] = w[i + q];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        total = __fadd_rn(total, t[q]);
-        S[i + q] = total;
-      }
-    }
-    for (; i < m; ++i) {
-      total = __fadd_rn(total, w[i]);
-      S[i] = total;
-    }
+  for (int i = 0; i < 32; ++i) {
+    const float wi = __shfl_sync(0xffffffffu, w_lo, i);
+    if (i < m) total = __fadd_rn(total, wi);
+    if (lane == i) s_lo = total;
   }
-  __syncwarp();
-  const float total = S[m - 1];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float wi = __shfl_sync(0xffffffffu, w_hi, i);
+    if (32 + i < m) total = __fadd_rn(total, wi);
+    if (lane == i) s_hi = total;
+  }
+  // S[i] for a per-lane index i (every lane calls)
+  auto S_at = [&](int i) -> float {
+    const float lo = __shfl_sync(0xffffffffu, s_lo, i & 31);
+    const float hi = __shfl_sync(0xffffffffu, s_hi, i & 31);
+    return i < 32 ? lo : hi;
+  };
   int cutoff = m;
   float target = 0.0f;
   if (a.p.top_p < 1.0f) {
-    target = __fmul_rn(total, a.p.top_p);
-    const unsigned b0 = __ballot_sync(0xffffffffu, lane < m && S[lane] >= target);
-    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < m && S[lane + 32] >= target);
+    target = __fmul_rn(total, a.p.top_p);  // total = S[m - 1]
+    const unsigned b0 = __ballot_sync(0xffffffffu, lane < m && s_lo >= target);
+    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < m && s_hi >= target);
     cutoff = b0 ? __ffs(b0) : (b1 ? 32 + __ffs(b1) : m);
   }
-  const float retained = S[cutoff - 1];
+  const float retained = S_at(cutoff - 1);
   const float sample = __fmul_rn(u, retained);
   int sel;
   {
-    const unsigned b0 = __ballot_sync(0xffffffffu, lane < cutoff && sample <= S[lane]);
-    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < cutoff && sample <= S[lane + 32]);
+    const unsigned b0 = __ballot_sync(0xffffffffu, lane < cutoff && sample <= s_lo);
+    const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < cutoff && sample <= s_hi);
     sel = b0 ? __ffs(b0) - 1 : (b1 ? 32 + __ffs(b1) - 1 : cutoff - 1);
   }
-  if (lane == 0) {
-    uint32_t f = any_slow ? FLAG_EXP_SLOW : 0u;
+  // boundary tests: lanes 0/1 the draw against S[sel] and S[sel - 1], lanes
+  // 2/3 the cutoff against S[cutoff - 1] and S[cutoff - 2]
+  const int ti = lane == 0 ? sel : lane == 1 ? sel - 1 : lane == 2 ? cutoff - 1 : cutoff - 2;
+  const float sv = S_at(ti > 0 ? ti : 0);
+  bool hit = false;
+  if (lane < 2) {
     const double tol = 1e-6 * (double)retained;
-    if (fabs((double)sample - (double)S[sel]) <= tol ||
-        (sel >= 1 && fabs((double)sample - (double)S[sel - 1]) <= tol))
-      f |= FLAG_DRAW_BOUNDARY;
-    if (a.p.top_p < 1.0f) {
-      const double tt = 1e-6 * (double)target;
-      if (fabs((double)S[cutoff - 1] - (double)target) <= tt ||
-          (cutoff >= 2 && fabs((double)S[cutoff - 2] - (double)target) <= tt))
-        f |= FLAG_CUTOFF_BOUNDARY;
-    }
-    if (a.flags) a.flags[row] = f;
+    hit = ti >= 0 && fabs((double)sample - (double)sv) <= tol;
+  } else if (lane < 4 && a.p.top_p < 1.0f) {
+    const double tt = 1e-6 * (double)target;
+    hit = ti >= 0 && fabs((double)sv - (double)target) <= tt;
   }
+  const unsigned fb = __ballot_sync(0xffffffffu, hit);
   // token and the tie flag from the sorted keys
   const int rs = sel >> 5, ls = sel & 31;
   uint64_t ksel = 0, kprev = 0, knext = 0;
@@ -303,15 +305,18 @@ __device__ __noinline__ void finish_weights_warp(const SampleArgs& a, int row, u
     const bool tie = (sel > 0 && (uint32_t)(kprev >> 32) == ks) ||
                      (sel + 1 < m && (uint32_t)(knext >> 32) == ks);
     a.tokens[row] = cand_id(ksel);
-    if (tie && a.flags) a.flags[row] |= FLAG_TIE_AT_DRAW;
+    if (a.flags) {
+      uint32_t f = any_slow ? FLAG_EXP_SLOW : 0u;
+      if (fb & 3u) f |= FLAG_DRAW_BOUNDARY;
+      if (fb & 12u) f |= FLAG_CUTOFF_BOUNDARY;
+      if (tie) f |= FLAG_TIE_AT_DRAW;
+      a.flags[row] = f;
+    }
   }
   if (a.probs) {
     float* prow = a.probs + (size_t)row * a.V;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int i = r * 32 + lane;
-      if (i < cutoff) prow[cand_id(k[r])] = __fdiv_rn(w[i], retained);
-    }
+    if (lane < cutoff) prow[cand_id(k[0])] = __fdiv_rn(w_lo, retained);
+    if (lane + 32 < cutoff) prow[cand_id(k[1])] = __fdiv_rn(w_hi, retained);
   }
 }
 
