@@ -40,7 +40,7 @@ constexpr int TL_WARPS = TL_THREADS / 32;
 constexpr int TL_UNROLL = 4;                       // float4 loads in flight per thread
 constexpr int TL_STEP = TL_THREADS * TL_UNROLL;    // float4 per CTA step
 constexpr int TL_KMAX = 64;
-constexpr int TL_WORK = 32768;                     // finish / merge / histogram / queue area
+constexpr int TL_WORK = 32768;                     // select / finish / merge area
 // Queued float4s per warp during the stream (value and index), in the
 // candidate-list and work areas (contiguous, 48 KiB, unused while streaming).
 constexpr int TL_QV = 152;
@@ -49,7 +49,8 @@ static_assert(TL_WARPS * TL_QV * 20 <= TK_CAPB * 8 + TL_WORK, "stream queues do 
 inline size_t tl_smem_bytes(int bm_words, int h_cap) {
   return (size_t)TL_WARPS * TW_WCAP * 8      // warp buffers
          + (size_t)TK_CAPB * 8               // compact candidate list
-         + (size_t)TL_WORK                   // finish / merge work, per-warp histograms
+         + (size_t)TL_WORK                   // select, finish and merge work
+                                             // (with the candidate list: stream queues)
          + 256 * 4                           // radix histogram
          + (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
@@ -64,10 +65,11 @@ constexpr int TL_LISTV = 512;  // float offset in cv of the lists' value keys (a
 // -inf, NaN and +inf must not be marked), via one histogram of TL_NB linear
 // bins over [lo, hi] (bin 0 holds the largest values).
 //  exact == false: returns a lower bound of the k-th largest (the smallest
-//                  value in its bin); *cnt_total = number of marked values.
+//                  value in its bin).
 //  exact == true : returns the k-th largest exactly; values of its bin are
-//                  ranked in shared memory (`tmp`, >= TL_WORK bytes minus the
-//                  histogram) and, when that bin is crowded, by a radix select.
+//                  ranked in shared memory (`work`, TL_WORK bytes: the bins,
+//                  then the bin's values) and, when that bin is crowded, by a
+//                  radix select (`hist256`, `sh`).
 // Returns -inf when fewer than k values are marked. All threads call.
 template <int N>
 __device__ float cta_select_linear(const float (&v)[N], const bool (&valid)[N], int k, bool exact,
