@@ -331,6 +331,22 @@ __device__ __forceinline__ void topk_ldg_body(const SampleArgs& a, int* owner) {
         }
       }
     }
+    // while the select below runs (no loads of this CTA in flight), each warp
+    // has L2 fetch its own part of the next two steps (bulk prefetch, no
+    // registers; the stream's loads of them then hit L2)
+    if (lane == 0 && hist_ok) {
+#pragma unroll
+      for (int st = 1; st <= 2; ++st)
+#pragma unroll
+        for (int u = 0; u < TL_UNROLL; ++u) {
+          const int q = st * TL_STEP + u * TL_THREADS + warp * 32;
+          const int e = min(n4, q + 32);
+          if (q < e)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(body + q),
+                         "r"((unsigned)(e - q) * 16u)
+                         : "memory");
+        }
+    }
     // the smallest maximum in the bin of the K-th largest maximum: distinct
     // elements of the segment, so a lower bound of its K-th largest value
     const float sv[1] = {tmax};
