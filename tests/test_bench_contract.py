@@ -1,0 +1,40 @@
+"""The benchmark's reference arm (CPU only): one JSON line on rank 0 with the
+headline metric, its CPU baseline and a zero-copy e2e entry; other ranks of a
+multi-process launch exit 0 without output."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(env_extra):
+    env = dict(os.environ, **env_extra)
+    p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                        "--steps", "2", "--warmup", "1"], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-2000:]
+    return [l for l in p.stdout.splitlines() if l.strip().startswith("{")]
+
+
+def test_reference_arm_prints_one_contract_line():
+    lines = _run({"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0"})
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    baseline = json.load(open(os.path.join(ROOT, "BASELINE.json")))
+    assert d["impl"] == "reference"
+    assert d["metric"] == baseline["metric"]
+    assert d["unit"] == "rows/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["steps"] == 2 and d["warmup"] == 1 and d["n_gpus"] == 1
+    assert d["config"]["B"] == 256 and d["config"]["V"] == 128256
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference")
+    assert cb["sample"]
+    e2e = d["e2e"]
+    assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_other_ranks_do_no_work():
+    assert _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
