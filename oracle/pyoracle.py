@@ -1,6 +1,6 @@
 """ctypes front end of the C oracle (oracle/sampler_oracle.c).
 
-TEST INFRASTRUCTURE ONLY: the checker for the CUDA kernels and the timed CPU
+TEST INFRASTRUCTURE ONLY: the oracle the CUDA kernels are tested against and the timed CPU
 stand-in for the reference's C# TokenSampler. The product package never
 imports this module.
 """

@@ -1,7 +1,7 @@
 """The reference's own CUDA library, Neuraval.Cuda.Native (navcuda.cu), compiled
 from its source for sm_100a by `make -C oracle ref` into oracle/_ref/.
 
-Test infrastructure only: the checker of the row softmax (the reference's
+Test infrastructure only: what the row-softmax tests compare against (the reference's
 ncb_cuda_softmax_rows_device, navcuda.cu:616-700). The compiled library travels
 with the repository copy; building it needs the reference source tree.
 """

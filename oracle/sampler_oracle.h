@@ -3,7 +3,7 @@
  *
  * TEST INFRASTRUCTURE ONLY. Nothing in the product library links, loads or
  * calls this code. Only the pytest suite, `__graft_entry__.smoke()` and the
- * CPU-baseline leg of `bench.py` use it, and only as the checker or as the
+ * CPU-baseline leg of `bench.py` use it, and only as the oracle to compare with or as the
  * timed CPU stand-in for the reference's C# implementation.
  *
  * It restates, in strict IEEE fp32 C, the C# reference:
