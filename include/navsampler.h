@@ -131,8 +131,10 @@ NCB_API int ncb_sample_rows(NcbSampler* sampler, const float* h_logits, int rows
  *   - Runs on the current device. The first call on a device looks up that
  *     array's device address (cudaGetSymbolAddress) and raises the kernels'
  *     shared-memory limits; make that first call before any stream capture.
- *   - Serves greedy rows and top-k <= 64 only; other options return
- *     NCB_ERROR_CAPACITY, as do rows > 1024 and vocab > 2^24. A row whose
+ *   - Serves greedy rows and top-k <= 64 with top_k < vocab only (top_k >=
+ *     vocab means "no top-k", the full-vocabulary nucleus, whose scratch
+ *     grows with rows x vocab); other options return NCB_ERROR_CAPACITY, as
+ *     do rows > 1024 and vocab > 2^24. A row whose
  *     frequency counting needs more than 4096 history ids comes back as
  *     token -1 with NCB_FLAG_BAD_HISTORY.
  *   - Every call reuses the same array (the parts that must start at zero are

@@ -785,7 +785,10 @@ extern "C" NCB_API int ncb_sample_rows_noalloc_device(const float* d_logits, int
   if (cudaMemsetAsync(nd.base + NA_OFF_ZERO, 0, NA_BYTES - NA_OFF_ZERO, stream) != cudaSuccess)
     return set_status(NCB_ERROR_LAUNCH_FAILED);
 
-  int S = choose_splits(rows, vocab, nd.num_sms, 0);
+  // top-k rows split like the handle path's (at most 8 segments, so a split
+  // row's merge holds K x S <= 512 candidates, within its 2048-entry buffer)
+  int S = prm->greedy ? choose_splits(rows, vocab, nd.num_sms, 0)
+                      : choose_splits_topk(rows, vocab, nd.num_sms, 0);
   if (rows * S > NA_MAX_SEGMENTS) S = NA_MAX_SEGMENTS / rows > 0 ? NA_MAX_SEGMENTS / rows : 1;
   a.seg_len = round_up((vocab + S - 1) / S, 4);
   S = (vocab + a.seg_len - 1) / a.seg_len;

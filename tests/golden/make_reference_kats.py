@@ -5,9 +5,10 @@ Sources (xUnit, Neuraval.Tests/):
   TokenSamplerTests.cs:10-93, LogitsProcessorTests.cs:9-156 (calls at :14-155),
   GenerationOptionsTests.cs:27-71.
 Each case records the file:line it comes from and a literal snippet of that
-line. When the reference tree is present (NEURAVAL_REFERENCE or
-/root/reference), this script checks that every snippet appears on the cited
-line before writing the fixture, so the transcription is pinned to the source.
+line. The script checks that every snippet appears on the cited line of the
+reference tree (its root in NEURAVAL_REFERENCE) before writing the fixture, so
+the transcription is pinned to the source:
+  NEURAVAL_REFERENCE=<reference root> python tests/golden/make_reference_kats.py
 The C# tests draw with `new Random(seed)`; the cases here only use draws that
 the reference pins for every seed (greedy, top-k 1), so any u gives the answer.
 """
@@ -113,12 +114,15 @@ def verify(root: str) -> int:
 
 
 def main() -> int:
-    root = os.environ.get("NEURAVAL_REFERENCE", "/root/reference")
-    if os.path.isdir(root):
-        bad = verify(root)
-        if bad:
-            return 1
-        print(f"verified {len(SAMPLER) + len(PROCESSOR) + len(OPTIONS)} citations against {root}")
+    root = os.environ.get("NEURAVAL_REFERENCE")
+    if not root or not os.path.isdir(root):
+        print("set NEURAVAL_REFERENCE to the reference tree's root: every citation is "
+              "checked against it before the fixture is written", file=sys.stderr)
+        return 1
+    bad = verify(root)
+    if bad:
+        return 1
+    print(f"verified {len(SAMPLER) + len(PROCESSOR) + len(OPTIONS)} citations against {root}")
     with open(OUT, "w") as fh:
         json.dump(dict(sampler=SAMPLER, processor=PROCESSOR, options=OPTIONS,
                        options_base=OPTIONS_BASE), fh, indent=1)
