@@ -3,19 +3,24 @@
 
 One step = one batched TokenSampler.SampleNext over a [256, 128256] fp32 logits
 batch (Zipf-ranked logits, 1024-id histories, repetition 1.15, T 0.7, top-k 50,
-top-p 0.9), i.e. the C ABI call ncb_sample_rows_device on device-resident inputs.
+top-p 0.9): the C ABI call ncb_sample_rows_device on device-resident inputs.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload zipf_ranked|vocab_sharded|softmax_rows] [--exchange nccl|peer]
+                  [--workload zipf_ranked|peaked_head|zipf_history_nucleus|
+                              high_entropy_nucleus|vocab_sharded|softmax_rows]
+                  [--exchange nccl|peer]
 
-N>1 runs under torch.distributed (one process per GPU, NCCL for the barrier and
-the max-over-ranks timing only): every rank samples its own batch (rows shard
-across GPUs with no data-path exchange), so scaling is weak.
+N>1 runs under torch.distributed, one process per GPU. The fixed 256-row batch
+is split over the GPUs by rows (sharding.row_range); each step every GPU
+samples its rows and one NCCL all-gather gives every GPU all 256 token ids and
+flags (strong scaling). Extra keys on the same line: every rank sampling its
+own 256-row batch with no exchange (weak replicas), the 128 x 262144 batch with
+its vocabulary split over the GPUs, the 1024 x 151936 nucleus batch split by
+rows, one-row latency through the host-array call, the host-to-device copy
+alone, and the parity of the sampled batch against the oracle.
 --impl reference times the reference's CPU sampler on the host: the C# code
-cannot run here (no .NET runtime), so its C restatement (oracle/) stands in.
-Other workloads: vocab_sharded (the 128 x 262144 batch with its vocabulary split
-over the GPUs, strong scaling) and softmax_rows (the row softmax of the 256 x
-128256 batch; its reference arm is the reference's own CUDA kernel).
+cannot run here (no .NET runtime), so its C restatement (oracle/) stands in,
+on the whole batch with every host thread.
 """
 from __future__ import annotations
 
@@ -49,15 +54,19 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--extras", type=int, default=1,
+                    help="headline only: 0 skips the extra measurements (replicas, "
+                         "vocabulary shards, nucleus batch, one-row latency)")
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
                     help="vocab_sharded: records exchanged by an NCCL all-gather, or through "
                          "peer memory by the shard kernel itself")
     ap.add_argument("--workload", default="zipf_ranked",
                     choices=["zipf_ranked", "peaked_head", "zipf_history_nucleus",
                              "high_entropy_nucleus", "vocab_sharded", "softmax_rows"],
-                    help="zipf_ranked: the headline (rows shard over GPUs); vocab_sharded: "
+                    help="zipf_ranked: the headline (rows split over GPUs); vocab_sharded: "
                          "128 x 262144, vocabulary split over GPUs; softmax_rows: row softmax "
-                         "of the 256 x 128256 logits batch")
+                         "of the 256 x 128256 logits batch; the others: their batch split "
+                         "over the GPUs by rows")
     return ap.parse_args()
 
 
@@ -68,24 +77,43 @@ def dist_env():
     return rank, world, local
 
 
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def workload(rank=0, name="zipf_ranked"):
-    """The batch of a sampling workload (the headline by default); rank r > 0 of
-    a multi-GPU run gets its own rows (same generator, another seed)."""
+    """The batch of a sampling workload (the headline by default); rank r > 0
+    gets its own rows (same generator, another seed) -- the weak replicas."""
     from neuraval_b200 import workloads
     gen = workloads.WORKLOADS[name]
     return gen() if rank == 0 else gen(seed=1000 * rank + 7)
 
 
-def config_of(wl, extra=None):
+def nbuf_for(rows, V, least=NBUF):
+    """Rotated input copies per GPU so that a copy is read again only after
+    twice the L2 capacity has streamed through."""
+    return max(least, -(-2 * L2_BYTES // max(1, rows * V * 4)))
+
+
+def rows_config(wl, world):
+    """The `config` of a rows-split line; identical in both arms of the bench."""
+    from neuraval_b200 import sharding
     B, V = wl["logits"].shape
     H = int(wl["hist_offsets"][-1] // B)
-    c = {"workload": wl["name"], "B": B, "V": V, "history_per_row": H,
-         **{k: v for k, v in wl["params"].items()},
-         "uniforms": "one seeded u in [0,1) per row",
-         "l2": f"inputs larger than L2: {NBUF} copies of the batch rotated across steps"}
-    if extra:
-        c.update(extra)
-    return c
+    lo, hi = sharding.row_range(B, world, 0)
+    nb = nbuf_for(hi - lo, V)
+    par = (f"{B} rows split over {world} GPUs (contiguous row ranges), token ids and flags "
+           "all-gathered over NCCL every step" if world > 1 else f"{B} rows on 1 GPU")
+    return {"workload": wl["name"], "B": B, "V": V, "history_per_row": H,
+            **{k: v for k, v in wl["params"].items()},
+            "uniforms": "one seeded u in [0,1) per row",
+            "parallelism": par,
+            "l2": (f"inputs larger than L2: each GPU rotates {nb} copies of its rows across "
+                   "steps (twice the L2 capacity between reuses); the CPU arm reads the whole "
+                   "batch, larger than its caches")}
 
 
 def measured_peak():
@@ -165,12 +193,15 @@ class ClockSampler:
                 "reasons": names, "samples": len(self.samples)}
 
 
+# ---- the oracle: timed CPU baseline and the parity checker (rank 0 only) ------
+
 def cpu_baseline(wl, seconds):
     """The oracle (C restatement of the C# sampler) on all host cores over a
-    bounded sample of the same workload; returns (rows/s, threads, sample desc, 1-thread rows/s)."""
+    bounded sample of the same workload; returns (rows/s, threads, sample desc,
+    1-thread rows/s)."""
     from oracle import pyoracle
     pyoracle.build()
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     p = pyoracle.make_params(**wl["params"])
     offs = np.asarray(wl["hist_offsets"], np.int64)
     B = wl["logits"].shape[0]
@@ -190,6 +221,40 @@ def cpu_baseline(wl, seconds):
     return rows / dt, threads, f"{rows} rows ({rows // B} full batches of {B}) in {dt:.1f} s", one
 
 
+def parity_of(wl, tokens, flags):
+    """Tokens and flags of the sampled batch against the oracle: bit for bit with
+    the correctly rounded exp the kernels use, and against libm expf (the
+    reference's MathF.Exp), where rows may differ only when a boundary or tie
+    flag is set; the flagged rows are counted."""
+    from neuraval_b200 import native
+    from oracle import pyoracle
+    pyoracle.build()
+    p = pyoracle.make_params(**wl["params"])
+    offs = np.asarray(wl["hist_offsets"], np.int64)
+    th = host_threads()
+    cmp = ~native.FLAG_EXP_SLOW & 0xFFFFFFFF
+    ct, cf, _ = pyoracle.sample_rows(wl["logits"], wl["hist_ids"], offs, wl["uniforms"], p,
+                                     exp_mode=pyoracle.EXP_CR, threads=th)
+    lt, lf, _ = pyoracle.sample_rows(wl["logits"], wl["hist_ids"], offs, wl["uniforms"], p,
+                                     exp_mode=pyoracle.EXP_GLIBC, threads=th)
+    tokens = np.asarray(tokens, np.int32)
+    flags = np.asarray(flags, np.uint32)
+    both = flags | lf
+    exempt = (both & native.PARITY_EXEMPT) != 0
+    differ = tokens != lt
+    return {"rows": int(tokens.size),
+            "exact_cr_rows_differ": int(((tokens != ct) | ((flags & cmp) != (cf & cmp))).sum()),
+            "flagged_boundary": int(((both & (native.FLAG_DRAW_BOUNDARY |
+                                              native.FLAG_CUTOFF_BOUNDARY)) != 0).sum()),
+            "flagged_tie": int(((both & native.FLAG_TIE_AT_DRAW) != 0).sum()),
+            "differ_unflagged": int((differ & ~exempt).sum()),
+            "differ_flagged": int((differ & exempt).sum()),
+            "nonfinite_or_overflow": int(((flags & (native.FLAG_NONFINITE |
+                                                    native.FLAG_TIES_OVERFLOW)) != 0).sum()),
+            "checker": "oracle/ (C restatement of TokenSampler.cs:54-135): exact with the "
+                       "correctly rounded exp; libm expf for the flag-exempt comparison"}
+
+
 def kernels_of(params, V):
     """The kernels one sampling call launches for these parameters (the
     dispatch of ncb_sample_rows_device): a name for the timed pair and the
@@ -205,37 +270,41 @@ def kernels_of(params, V):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle port of TokenSampler on the host's cores,
+    the whole batch every step, rank 0 only."""
     if rank != 0:
         return 0
     if args.workload == "softmax_rows":
         return run_softmax_reference(args)
-    wl = workload(0, args.workload)
+    name = "zipf_ranked" if args.workload == "zipf_ranked" else args.workload
+    wl = workload(0, name)
     from oracle import pyoracle
     pyoracle.build()
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     p = pyoracle.make_params(**wl["params"])
     offs = np.asarray(wl["hist_offsets"], np.int64)
     B = wl["logits"].shape[0]
-    rows_per_step = min(B, 8 * threads)  # bounded sample per step
-    lg = wl["logits"][:rows_per_step]
-    h = wl["hist_ids"][: offs[rows_per_step]]
-    o = offs[: rows_per_step + 1]
-    u = wl["uniforms"][:rows_per_step]
+    lg, h, u = wl["logits"], wl["hist_ids"], wl["uniforms"]
     for _ in range(args.warmup):
-        pyoracle.sample_rows(lg, h, o, u, p, exp_mode=pyoracle.EXP_GLIBC, threads=threads)
+        pyoracle.sample_rows(lg, h, offs, u, p, exp_mode=pyoracle.EXP_GLIBC, threads=threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        pyoracle.sample_rows(lg, h, o, u, p, exp_mode=pyoracle.EXP_GLIBC, threads=threads)
+        pyoracle.sample_rows(lg, h, offs, u, p, exp_mode=pyoracle.EXP_GLIBC, threads=threads)
     dt = time.perf_counter() - t0
-    value = rows_per_step * args.steps / dt
-    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+    value = B * args.steps / dt
+    metric = METRIC if name == "zipf_ranked" else f"sampled rows/sec, {wl['name']}"
+    cfg = (rows_config(wl, world) if name != "vocab_sharded" else
+           {"workload": wl["name"], "B": B, "V": wl["logits"].shape[1]})
+    out = {"impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-           "data": "synthetic", "config": config_of(wl, {"rows_per_step": rows_per_step}),
+           "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+           "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic (seeded generator, no dataset)", "config": cfg,
            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                            "sample": f"{rows_per_step} rows of the batch per step, {args.steps} steps; "
-                                      "C restatement of TokenSampler.SampleFiltered (libm expf); "
-                                      "the C# original needs a .NET runtime, absent here"},
+                            "sample": f"the whole {B}-row batch every step, {args.steps} steps, "
+                                      f"{threads} threads; C restatement of "
+                                      "TokenSampler.SampleFiltered (libm expf); the C# "
+                                      "original needs a .NET runtime, absent here"},
            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
     return 0
@@ -261,8 +330,10 @@ def main():
             out = run_vocab_sharded(args, rank, world, dev)
         elif args.workload == "softmax_rows":
             out = run_softmax(args, rank, world, dev)
+        elif args.workload == "zipf_ranked":
+            out = run_headline(args, rank, world, dev)
         else:
-            out = run_rows(args, rank, world, dev)
+            out = run_rows_line(args, rank, world, dev, args.workload)
         if rank == 0:
             print(json.dumps(out), flush=True)
     finally:
@@ -272,140 +343,358 @@ def main():
     return 0
 
 
-def run_rows(args, rank, world, dev):
-    """The headline: every rank samples its own 256-row batch (rows shard with
-    no exchange), timed as one replay of a CUDA graph holding the K steps."""
+# ---- rows split over the GPUs ---------------------------------------------------
+
+def time_graph(fn, steps, dev, world, clocks=None):
+    """`fn(i)` for i < steps captured once in a CUDA graph, one untimed replay,
+    then one replay between CUDA events on the current stream (ms)."""
     import torch
-    from neuraval_b200 import native, sharding, workloads
-    from neuraval_b200.sampler import CudaTokenSampler
-
-    wl = workload(rank, args.workload)
-    B, V = wl["logits"].shape
-    H = int(wl["hist_offsets"][-1] // B)
-    params = native.make_params(**wl["params"])
-    sampler = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=V, max_history=H)
-    nbuf = max(NBUF, -(-2 * L2_BYTES // max(1, B * V * 4)))  # rotated copies span 2 x L2
-
-    bufs = []
-    for i in range(nbuf):
-        lg = torch.from_numpy(wl["logits"]).to(dev)
-        if i:
-            lg = lg.roll(i, dims=0) if B > 1 else lg.roll(i * 97, dims=1)  # distinct copies
-        bufs.append(lg.contiguous())
-    hist = torch.from_numpy(wl["hist_ids"]).to(dev)
-    offs = torch.from_numpy(wl["hist_offsets"]).to(dev)
-    u = torch.from_numpy(wl["uniforms"]).to(dev)
-    tokens = torch.empty(B, dtype=torch.int32, device=dev)
-    flags = torch.empty(B, dtype=torch.int32, device=dev)
-
-    def step(i, stream):
-        sampler.sample_rows_device(bufs[i % nbuf], hist, offs, u, params, tokens, flags,
-                                   None, stream)
-
     cur = torch.cuda.current_stream(dev)
-    for i in range(max(3, args.warmup)):
-        step(i, cur)
-    torch.cuda.synchronize()
-
-    # eager launches (each call goes through ctypes): reported for reference
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(cur)
-    for i in range(args.steps):
-        step(i, cur)
-    e1.record(cur)
-    torch.cuda.synchronize()
-    eager_ms = e0.elapsed_time(e1)
-
-    # timed region: the K steps captured once in a CUDA graph and replayed, so the
-    # device timeline holds only the sampling kernels (no host launch gaps)
     graph = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(cur)
     with torch.cuda.stream(cap):
         with torch.cuda.graph(graph, stream=cap):
-            for i in range(args.steps):
-                step(i, torch.cuda.current_stream(dev))
+            for i in range(steps):
+                fn(i)
     torch.cuda.synchronize()
-    graph.replay()  # one untimed replay
+    graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(dev.index)
-    with clocks:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(cur)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with (clocks if clocks is not None else contextlib.nullcontext()):
+        t0.record(cur)
         graph.replay()
-        t_end.record(cur)
+        t1.record(cur)
         torch.cuda.synchronize()
-    total_ms, eager_ms = sharding.max_over_ranks([t_start.elapsed_time(t_end), eager_ms], dev)
-    per_launch_ms = total_ms / args.steps
-    value = world * B * args.steps / (total_ms / 1e3)
-    del graph
+    del graph  # graphs holding NCCL calls go before the process group
+    return t0.elapsed_time(t1)
 
-    # end to end through the host-array entry point (pinned host buffers)
-    e2e = None
-    if args.e2e_steps > 0:
-        h_logits = torch.from_numpy(wl["logits"]).pin_memory().numpy()
-        h_hist = torch.from_numpy(wl["hist_ids"]).pin_memory().numpy()
-        h_offs = torch.from_numpy(wl["hist_offsets"]).pin_memory().numpy()
-        h_u = torch.from_numpy(wl["uniforms"]).pin_memory().numpy()
-        for _ in range(2):
-            sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
-        if world > 1:
-            torch.distributed.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            sampler.sample_rows(h_logits, h_hist, h_offs, h_u, params)
-        (e2e_s,) = sharding.max_over_ranks([time.perf_counter() - t0], dev)
-        e2e = {"value": world * B * args.e2e_steps / e2e_s, "unit": UNIT,
-               "h2d_bytes_per_step": int(h_logits.nbytes + h_hist.nbytes + h_offs.nbytes +
-                                         h_u.nbytes),
-               "d2h_bytes_per_step": int(B * 4 * 2),
-               "api": "ncb_sample_rows (host arrays; copies in, samples, synchronises, "
-                      "copies out)"}
+
+class RowSplit:
+    """One GPU's share of a row-split batch: its rows on the device (rotated
+    copies), its sampler, and the all-gather of every GPU's tokens and flags."""
+
+    def __init__(self, wl, rank, world, dev, least_buffers=NBUF):
+        import torch
+        from neuraval_b200 import native, sharding
+        from neuraval_b200.sampler import CudaTokenSampler
+        self.wl, self.world, self.dev = wl, world, dev
+        B, V = wl["logits"].shape
+        self.B, self.V = B, V
+        self.H = int(wl["hist_offsets"][-1] // B)
+        lo, hi = sharding.row_range(B, world, rank)
+        self.lo, self.rows = lo, hi - lo
+        offs = np.asarray(wl["hist_offsets"], np.int64)
+        self.params = native.make_params(**wl["params"])
+        self.sampler = CudaTokenSampler(device=dev.index, max_rows=max(1, self.rows),
+                                        max_vocab=V, max_history=max(1, self.H))
+        mine = wl["logits"][lo:hi]
+        self.nbuf = nbuf_for(max(1, self.rows), V, least_buffers)
+        base = torch.from_numpy(np.ascontiguousarray(mine)).to(dev)
+        self.bufs = [base] + [
+            (base.roll(i, dims=0) if self.rows > 1 else base.roll(i * 97, dims=1)).contiguous()
+            for i in range(1, self.nbuf)]
+        h = wl["hist_ids"][offs[lo]: offs[hi]]
+        self.hist = torch.from_numpy(np.ascontiguousarray(h if h.size else np.zeros(1, np.int32),
+                                                          dtype=np.int32)).to(dev)
+        self.offs = torch.from_numpy((offs[lo: hi + 1] - offs[lo]).astype(np.int32)).to(dev)
+        self.u = torch.from_numpy(np.ascontiguousarray(wl["uniforms"][lo:hi])).to(dev)
+        # world > 1: the library's row-split sampler (its rows, then one NCCL
+        # all-gather of every GPU's tokens and flags)
+        self.split = sharding.RowShardedSampler(self.sampler, B) if world > 1 else None
+        self.local = torch.zeros((2, max(1, self.rows)), dtype=torch.int32, device=dev)
+
+    def step(self, i):
+        import torch
+        if self.split is not None:
+            self.split.sample(self.bufs[i % self.nbuf], self.hist, self.offs, self.u,
+                              self.params)
+        else:
+            self.sampler.sample_rows_device(self.bufs[i % self.nbuf], self.hist, self.offs,
+                                            self.u, self.params, self.local[0], self.local[1],
+                                            None, torch.cuda.current_stream(self.dev))
+
+    def tokens_flags(self):
+        """Every row's token and flags of the last step, in batch order (host)."""
+        if self.split is not None:
+            tok, fl = self.split.tokens_flags()
+        else:
+            tok, fl = self.local[0], self.local[1]
+        return tok.cpu().numpy(), fl.cpu().numpy().astype(np.uint32)
+
+    def close(self):
+        self.sampler.close()
+
+
+def run_split(wl, args, rank, world, dev, steps, clocks=None, least_buffers=NBUF):
+    """Times `steps` steps of the row-split batch (graph replay, max over ranks),
+    then samples the unrotated batch once more for the parity check.
+    Returns (ms for the steps, eager ms, tokens, flags, RowSplit)."""
+    import torch
+    from neuraval_b200 import sharding
+    rs = RowSplit(wl, rank, world, dev, least_buffers)
+    for i in range(max(3, args.warmup)):
+        rs.step(i)
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for i in range(steps):
+        rs.step(i)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1)
+    total_ms = time_graph(rs.step, steps, dev, world, clocks)
+    total_ms, eager_ms = sharding.max_over_ranks([total_ms, eager_ms], dev)
+    rs.step(0)  # the batch itself (copy 0), every rank: the step holds a collective
+    torch.cuda.synchronize()
+    tok, fl = rs.tokens_flags()
+    return total_ms, eager_ms, tok, fl, rs
+
+
+def run_headline(args, rank, world, dev):
+    """The headline line: the fixed 256 x 128256 batch split over the GPUs by
+    rows, plus the extra measurements."""
+    import torch
+    from neuraval_b200 import sharding, workloads
+    wl = workload(0, "zipf_ranked")
+    B, V = wl["logits"].shape
+    H = int(wl["hist_offsets"][-1] // B)
+    clocks = ClockSampler(dev.index)
+    total_ms, eager_ms, tok, fl, rs = run_split(wl, args, rank, world, dev, args.steps, clocks)
+    nbuf = rs.nbuf
+    rows_here = rs.rows
+    per_step_ms = total_ms / args.steps
+    value = B * args.steps / (total_ms / 1e3)
 
     out = None
+    extras = {}
+    if args.e2e_steps > 0:
+        extras["e2e"] = e2e_rows(rs, args, world, dev)
+    rs.close()
+    del rs
+    torch.cuda.empty_cache()
+    if args.extras:
+        extras["replicas"] = weak_replicas(args, rank, world, dev)
+        torch.cuda.empty_cache()
+        extras["vocab_sharded"] = vocab_sharded_summary(args, rank, world, dev)
+        torch.cuda.empty_cache()
+        extras["high_entropy_nucleus"] = nucleus_split_summary(args, rank, world, dev)
+        torch.cuda.empty_cache()
+        if world > 1:
+            torch.distributed.barrier()
+        if rank == 0:
+            extras["e2e_b1"] = e2e_one_row(dev)
+        if world > 1:
+            torch.distributed.barrier()
+
     if rank == 0:
         peak, peak_kind = measured_peak()
-        bytes_per_launch = B * workloads.bytes_per_row(V, H)
-        achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
+        rows_max = sharding.row_range(B, world, 0)[1]  # the largest share
+        bytes_per_launch = rows_max * workloads.bytes_per_row(V, H)
+        achieved = bytes_per_launch / (per_step_ms / 1e3) / 1e9
         kernel, launches = kernels_of(wl["params"], V)
         out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-               "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
-               "config": config_of(wl, {"parallelism": f"rows sharded, {world} GPU(s) x {B} rows"
-                                                       ", no exchange",
-                                        "l2": f"inputs larger than L2: {nbuf} copies of the "
-                                              "batch rotated across steps"}),
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step_ms,
+               "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+               "vs_baseline": None, "dtype": "fp32",
+               "data": "synthetic (seeded generator, no dataset)",
+               "config": rows_config(wl, world),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "peak_source": peak_kind,
-                            "traffic": profiled_traffic() if wl["name"].startswith("zipf_ranked")
-                            else None,
-                            "kernel": kernel,
-                            "algorithmic_bytes_per_launch": bytes_per_launch},
-               "e2e": e2e,
+                            "traffic": profiled_traffic() if world == 1 else None,
+                            "kernel": kernel + (" and the NCCL gather of the tokens, per step"
+                                                if world > 1 else ""),
+                            "algorithmic_bytes_per_launch": bytes_per_launch,
+                            "per_gpu_rows": rows_max},
                "gpu_launches": launches * args.steps,
-               "eager_value": world * B * args.steps / (eager_ms / 1e3),
-               "timing": "CUDA events around one replay of a CUDA graph holding the K steps; "
-                         "max over ranks",
-               "clocks": clocks.summary()}
+               "eager_value": B * args.steps / (eager_ms / 1e3),
+               "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
+                         "(the token all-gather included); max over ranks",
+               "clocks": clocks.summary(),
+               "parity": parity_of(wl, tok, fl)}
+        out["e2e"] = extras.pop("e2e", None)
+        out.update(extras)
         if world == 1 and args.cpu_seconds > 0:
             v, cores, sample, one = cpu_baseline(wl, args.cpu_seconds)
             out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                                    "sample": sample, "single_thread_value": one}
-    sampler.close()
     return out
 
 
-def run_vocab_sharded(args, rank, world, dev):
+def e2e_rows(rs, args, world, dev):
+    """End to end through the host-array call ncb_sample_rows: every step copies
+    this GPU's rows in from pinned host memory, samples, synchronises and copies
+    the tokens and flags out. Also the host-to-device copy of the same bytes
+    alone, for comparison."""
+    import torch
+    from neuraval_b200 import sharding
+    wl, lo, rows = rs.wl, rs.lo, rs.rows
+    offs = np.asarray(wl["hist_offsets"], np.int64)
+    h_logits = torch.from_numpy(np.ascontiguousarray(wl["logits"][lo: lo + rows])).pin_memory()
+    h_hist = torch.from_numpy(np.ascontiguousarray(
+        wl["hist_ids"][offs[lo]: offs[lo + rows]])).pin_memory()
+    h_offs = torch.from_numpy((offs[lo: lo + rows + 1] - offs[lo]).astype(np.int32)).pin_memory()
+    h_u = torch.from_numpy(np.ascontiguousarray(wl["uniforms"][lo: lo + rows])).pin_memory()
+    hl, hh, ho, hu = (t.numpy() for t in (h_logits, h_hist, h_offs, h_u))
+    for _ in range(2):
+        rs.sampler.sample_rows(hl, hh, ho, hu, rs.params)
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        rs.sampler.sample_rows(hl, hh, ho, hu, rs.params)
+    e2e_s = time.perf_counter() - t0
+    # the host-to-device copy alone (pinned, one copy per step)
+    d = torch.empty(h_logits.shape, dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        d.copy_(h_logits, non_blocking=True)
+        s.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            d.copy_(h_logits, non_blocking=True)
+            s.synchronize()
+        h2d_s = time.perf_counter() - t0
+    e2e_s, h2d_s = sharding.max_over_ranks([e2e_s, h2d_s], dev)
+    B = rs.B
+    return {"value": B * args.e2e_steps / e2e_s, "unit": UNIT,
+            "h2d_bytes_per_step": int(hl.nbytes + hh.nbytes + ho.nbytes + hu.nbytes),
+            "d2h_bytes_per_step": int(rows * 4 * 2),
+            "api": "ncb_sample_rows (host arrays; copies in, samples, synchronises, copies out); "
+                   "each GPU its own rows, max over ranks",
+            "ms_per_step": e2e_s / args.e2e_steps * 1e3,
+            "h2d_only_ms_per_step": h2d_s / args.e2e_steps * 1e3,
+            "h2d_only_gbs": hl.nbytes / (h2d_s / args.e2e_steps) / 1e9}
+
+
+def e2e_one_row(dev):
+    """The drop-in where the reference calls it: one 1 x 32000 row per call
+    (TextGenerator.cs:93) through ncb_sample_rows with host arrays, against the
+    oracle port on one thread (the reference's model: one call, one thread)."""
+    import torch
+    from neuraval_b200 import native, workloads
+    from neuraval_b200.sampler import CudaTokenSampler
+    from oracle import pyoracle
+    wl = workloads.peaked_head(B=1)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+    lg, hi, of, u = (pin(wl["logits"]), pin(wl["hist_ids"]), pin(wl["hist_offsets"]),
+                     pin(wl["uniforms"]))
+    p = native.make_params(**wl["params"])
+    n = 300
+    with CudaTokenSampler(device=dev.index, max_rows=1, max_vocab=32000, max_history=64) as s:
+        for _ in range(20):
+            s.sample_rows(lg, hi, of, u, p)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            tok, _, _ = s.sample_rows(lg, hi, of, u, p)
+        gpu_us = (time.perf_counter() - t0) / n * 1e6
+    pyoracle.build()
+    op = pyoracle.make_params(**wl["params"])
+    offs = np.asarray(wl["hist_offsets"], np.int64)
+    for _ in range(5):
+        pyoracle.sample_rows(wl["logits"], wl["hist_ids"], offs, wl["uniforms"], op,
+                             exp_mode=pyoracle.EXP_GLIBC, threads=1)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        ot, _, _ = pyoracle.sample_rows(wl["logits"], wl["hist_ids"], offs, wl["uniforms"], op,
+                                        exp_mode=pyoracle.EXP_GLIBC, threads=1)
+    cpu_us = (time.perf_counter() - t0) / n * 1e6
+    return {"workload": wl["name"], "us_per_call": gpu_us, "cpu_single_thread_us_per_row": cpu_us,
+            "same_token": bool(tok[0] == ot[0]),
+            "api": "ncb_sample_rows, host arrays (pinned), 1 row: copy in, sample, synchronise, "
+                   "copy out"}
+
+
+def weak_replicas(args, rank, world, dev):
+    """Every rank samples its own 256-row batch (same generator, its own seed):
+    no exchange; whole-job rows/s (weak scaling)."""
+    import torch
+    wl = workload(rank, "zipf_ranked")
+    # one "world" of one: each rank alone, no gather
+    total_ms, _, _, _, rs = run_split(wl, args, 0, 1, dev, args.steps)
+    from neuraval_b200 import sharding
+    (total_ms,) = sharding.max_over_ranks([total_ms], dev)
+    rs.close()
+    B = wl["logits"].shape[0]
+    return {"value": world * B * args.steps / (total_ms / 1e3), "unit": UNIT,
+            "ms_per_step": total_ms / args.steps, "scaling": "weak",
+            "parallelism": f"{world} GPU(s), each its own {B}-row batch, no exchange"}
+
+
+def nucleus_split_summary(args, rank, world, dev):
+    """The 1024 x 151936 high-entropy nucleus batch (no top-k) split by rows."""
+    from neuraval_b200 import workloads
+    wl = workloads.high_entropy_nucleus()
+    steps = max(3, min(args.steps, 40))
+    total_ms, _, tok, fl, rs = run_split(wl, args, rank, world, dev, steps, least_buffers=2)
+    rs.close()
+    B, V = wl["logits"].shape
+    H = int(wl["hist_offsets"][-1] // B)
+    out = None
+    if rank == 0:
+        from neuraval_b200 import sharding
+        peak, _ = measured_peak()
+        rows_max = sharding.row_range(B, world, 0)[1]
+        ach = rows_max * workloads.bytes_per_row(V, H) / (total_ms / steps / 1e3) / 1e9
+        out = {"value": B * steps / (total_ms / 1e3), "unit": UNIT, "steps": steps,
+               "ms_per_step": total_ms / steps, "hbm_frac": ach / peak,
+               "kernel": kernels_of(wl["params"], V)[0],
+               "config": rows_config(wl, world), "parity": parity_of(wl, tok, fl)}
+    return out
+
+
+def run_rows_line(args, rank, world, dev, name):
+    """A secondary workload as its own line, split over the GPUs by rows."""
+    from neuraval_b200 import sharding, workloads
+    wl = workload(0, name)
+    B, V = wl["logits"].shape
+    H = int(wl["hist_offsets"][-1] // B)
+    clocks = ClockSampler(dev.index)
+    total_ms, eager_ms, tok, fl, rs = run_split(wl, args, rank, world, dev, args.steps, clocks)
+    rs.close()
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peak()
+    rows_max = sharding.row_range(B, world, 0)[1]
+    per_step_ms = total_ms / args.steps
+    bytes_per_launch = rows_max * workloads.bytes_per_row(V, H)
+    achieved = bytes_per_launch / (per_step_ms / 1e3) / 1e9
+    kernel, launches = kernels_of(wl["params"], V)
+    out = {"metric": f"sampled rows/sec, {wl['name']}", "value": B * args.steps / (total_ms / 1e3),
+           "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": per_step_ms, "higher_is_better": True,
+           "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic (seeded generator, no dataset)", "config": rows_config(wl, world),
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                        "kernel": kernel, "algorithmic_bytes_per_launch": bytes_per_launch},
+           "e2e": None, "gpu_launches": launches * args.steps,
+           "eager_value": B * args.steps / (eager_ms / 1e3),
+           "timing": "CUDA events around one replay of a CUDA graph holding the K steps; "
+                     "max over ranks",
+           "clocks": clocks.summary(), "parity": parity_of(wl, tok, fl)}
+    if world == 1 and args.cpu_seconds > 0:
+        v, cores, sample, one = cpu_baseline(wl, args.cpu_seconds)
+        out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                               "sample": sample, "single_thread_value": one}
+    return out
+
+
+# ---- vocabulary split over the GPUs ----------------------------------------------
+
+def vocab_sharded_measure(args, rank, world, dev, clocks=None):
     """The 128 x 262144 batch (top-k 64) with its vocabulary split over the ranks:
     per step, the shard candidate kernel, one NCCL all-gather of the records and
     the merge kernel on every rank. Total work is fixed (strong scaling). The
     K steps are captured in one CUDA graph (the all-gather included) and
-    replayed; each part is also timed alone the same way."""
+    replayed; each part is also timed alone the same way. Returns a dict of
+    the measured numbers (rank 0) and the tokens' check against one GPU."""
     import torch
     from neuraval_b200 import native, sharding, workloads
     from neuraval_b200.sampler import CudaTokenSampler
@@ -460,48 +749,23 @@ def run_vocab_sharded(args, rank, world, dev):
             exchange(i)
             merge(i)
 
-    cur = torch.cuda.current_stream(dev)
     for i in range(max(3, args.warmup)):
         full(i)
     torch.cuda.synchronize()
-
-    def timed(fn, clocks=None):
-        graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(dev)
-        cap.wait_stream(cur)
-        with torch.cuda.stream(cap):
-            with torch.cuda.graph(graph, stream=cap):
-                for i in range(args.steps):
-                    fn(i)
-        torch.cuda.synchronize()
-        graph.replay()  # one untimed replay
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with (clocks if clocks is not None else contextlib.nullcontext()):
-            t0.record(cur)
-            graph.replay()
-            t1.record(cur)
-            torch.cuda.synchronize()
-        del graph  # graphs holding NCCL calls go before the process group
-        return t0.elapsed_time(t1)
-
-    clocks = ClockSampler(dev.index)
-    total_ms = timed(full, clocks)
+    total_ms = time_graph(full, args.steps, dev, world, clocks)
     if peer is not None:
         # a merge alone re-reads the last call's records (its flags are already set)
-        parts = [timed(candidates), 0.0, timed(merge)]
+        parts = [time_graph(candidates, args.steps, dev, world), 0.0,
+                 time_graph(merge, args.steps, dev, world)]
         parts[1] = max(0.0, total_ms - parts[0] - parts[2])
     else:
-        parts = [timed(candidates), timed(exchange), timed(merge)]
+        parts = [time_graph(f, args.steps, dev, world) for f in (candidates, exchange, merge)]
     total_ms, *parts = sharding.max_over_ranks([total_ms] + parts, dev)
-    # the sampled tokens equal the single-GPU sampler's on the whole rows
-    ok = True
     full(0)  # every rank: the step holds a collective
     torch.cuda.synchronize()
+    res = None
     if rank == 0:
+        # the sampled tokens equal the single-GPU sampler's on the whole rows
         ref_s = CudaTokenSampler(device=dev.index, max_rows=B, max_vocab=V, max_history=H)
         full_logits = torch.from_numpy(wl["logits"]).to(dev)
         rt = torch.empty_like(tokens)
@@ -511,42 +775,75 @@ def run_vocab_sharded(args, rank, world, dev):
         ok = bool(torch.equal(rt, tokens) and torch.equal(rf, flags))
         ref_s.close()
         del full_logits
-    out = None
-    if rank == 0:
-        peak, peak_kind = measured_peak()
-        per_gpu_bytes = B * (4 * width + 4 * H + 8)
-        per_step_s = total_ms / args.steps / 1e3
-        out = {"metric": "sampled rows/sec, vocabulary split over GPUs", "value":
-               B * args.steps / (total_ms / 1e3), "unit": UNIT, "n_gpus": world,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-               "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
-               "config": config_of(wl, {"parallelism": f"vocabulary sharded over {world} GPU(s);"
-                                                       f" {args.exchange} record exchange",
-                                        "l2": f"{nbuf} rotated copies of each shard",
-                                        "shard_columns": width,
-                                        "record_bytes_per_rank": B * sampler.shard_record_bytes}),
-               "parts_us_per_step": {"candidates": parts[0] / args.steps * 1e3,
-                                     "exchange": parts[1] / args.steps * 1e3,
-                                     "merge": parts[2] / args.steps * 1e3},
-               "exchange": ("records stored into every GPU's exchange area over NVLink by the "
-                            "library (epoch flags and acks)" if peer is not None else
-                            "NCCL all-gather of the records"),
-               "tokens_match_single_gpu": ok,
-               "roofline": {"bound": "hbm", "achieved": per_gpu_bytes / per_step_s / 1e9,
-                            "peak": peak, "unit": "GB/s",
-                            "frac": per_gpu_bytes / per_step_s / 1e9 / peak,
-                            "peak_source": peak_kind, "traffic": None,
-                            "kernel": "shard candidate kernel + all-gather + merge, per step",
-                            "algorithmic_bytes_per_launch": per_gpu_bytes},
-               "e2e": None,
-               "gpu_launches": (3 if peer is not None else 2) * args.steps,
-               "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
-                         "(all-gather included); max over ranks",
-               "clocks": clocks.summary()}
+        res = dict(wl=wl, B=B, V=V, H=H, width=width, nbuf=nbuf, total_ms=total_ms, parts=parts,
+                   ok=ok, record_bytes=sampler.shard_record_bytes,
+                   tokens=tokens.cpu().numpy(), flags=flags.cpu().numpy().astype(np.uint32))
     sampler.close()
-    return out
+    return res
 
+
+def vocab_sharded_summary(args, rank, world, dev):
+    r = vocab_sharded_measure(args, rank, world, dev)
+    if rank != 0:
+        return None
+    s = args.steps
+    return {"value": r["B"] * s / (r["total_ms"] / 1e3), "unit": UNIT,
+            "ms_per_step": r["total_ms"] / s, "n_gpus": world, "shard_columns": r["width"],
+            "parts_us_per_step": {"candidates": r["parts"][0] / s * 1e3,
+                                  "exchange": r["parts"][1] / s * 1e3,
+                                  "merge": r["parts"][2] / s * 1e3},
+            "exchange": "NCCL all-gather of the records" if args.exchange == "nccl" else
+                        "records stored into every GPU's exchange area over NVLink",
+            "tokens_match_single_gpu": r["ok"],
+            "parity": parity_of(r["wl"], r["tokens"], r["flags"]),
+            "config": {"workload": r["wl"]["name"], "B": r["B"], "V": r["V"],
+                       "parallelism": f"vocabulary split over {world} GPU(s)"}}
+
+
+def run_vocab_sharded(args, rank, world, dev):
+    clocks = ClockSampler(dev.index)
+    r = vocab_sharded_measure(args, rank, world, dev, clocks)
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peak()
+    B, H, width = r["B"], r["H"], r["width"]
+    per_gpu_bytes = B * (4 * width + 4 * H + 8)
+    per_step_s = r["total_ms"] / args.steps / 1e3
+    parts = r["parts"]
+    return {"metric": "sampled rows/sec, vocabulary split over GPUs", "value":
+            B * args.steps / (r["total_ms"] / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["total_ms"] / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic (seeded generator, no dataset)",
+            "config": {"workload": r["wl"]["name"], "B": B, "V": r["V"], "history_per_row": H,
+                       **r["wl"]["params"],
+                       "parallelism": f"vocabulary sharded over {world} GPU(s); "
+                                      f"{args.exchange} record exchange",
+                       "l2": f"{r['nbuf']} rotated copies of each shard",
+                       "shard_columns": width,
+                       "record_bytes_per_rank": B * r["record_bytes"]},
+            "parts_us_per_step": {"candidates": parts[0] / args.steps * 1e3,
+                                  "exchange": parts[1] / args.steps * 1e3,
+                                  "merge": parts[2] / args.steps * 1e3},
+            "exchange": ("records stored into every GPU's exchange area over NVLink by the "
+                         "library (epoch flags and acks)" if args.exchange == "peer" else
+                         "NCCL all-gather of the records"),
+            "tokens_match_single_gpu": r["ok"],
+            "parity": parity_of(r["wl"], r["tokens"], r["flags"]),
+            "roofline": {"bound": "hbm", "achieved": per_gpu_bytes / per_step_s / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": per_gpu_bytes / per_step_s / 1e9 / peak,
+                         "peak_source": peak_kind, "traffic": None,
+                         "kernel": "shard candidate kernel + all-gather + merge, per step",
+                         "algorithmic_bytes_per_launch": per_gpu_bytes},
+            "e2e": None,
+            "gpu_launches": (3 if args.exchange == "peer" else 2) * args.steps,
+            "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
+                      "(all-gather included); max over ranks",
+            "clocks": clocks.summary()}
+
+
+# ---- row softmax ------------------------------------------------------------------
 
 SOFTMAX_METRIC = "softmax rows/sec at B×V=256×128256 fp32"
 
@@ -576,31 +873,12 @@ def run_softmax(args, rank, world, dev):
                                          ctypes.c_void_p(out.data_ptr()), B, V, st)
         assert rc == 0, rc
 
-    cur = torch.cuda.current_stream(dev)
     for i in range(max(3, args.warmup)):
         step(i)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    cap = torch.cuda.Stream(dev)
-    cap.wait_stream(cur)
-    with torch.cuda.stream(cap):
-        with torch.cuda.graph(graph, stream=cap):
-            for i in range(args.steps):
-                step(i)
-    torch.cuda.synchronize()
-    graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
     clocks = ClockSampler(dev.index)
-    with clocks:
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(cur)
-        graph.replay()
-        t1.record(cur)
-        torch.cuda.synchronize()
-    (total_ms,) = sharding.max_over_ranks([t0.elapsed_time(t1)], dev)
-    del graph
+    total_ms = time_graph(step, args.steps, dev, world, clocks)
+    (total_ms,) = sharding.max_over_ranks([total_ms], dev)
     if rank != 0:
         return None
     peak, peak_kind = measured_peak()

@@ -66,6 +66,70 @@ def max_over_ranks(values: Sequence[float], device=None, group=None) -> list[flo
     return [float(x) for x in t.cpu()]
 
 
+class RowShardedSampler:
+    """Batched SampleNext over a batch split by rows (`row_range`), one range per rank.
+
+    Every rank calls `sample` with its own rows (logits, CSR history and
+    uniforms of those rows only) and gets every rank's tokens and flags: one
+    all-gather of 2 x ceil(rows / world) int32 per rank (NCCL over NVLink on
+    GPUs). The sampling itself needs no exchange: rows are independent
+    (TokenSampler.SampleNext samples one row at a time).
+    """
+
+    def __init__(self, sampler, rows: int, group=None):
+        import torch
+        import torch.distributed as dist
+        self.sampler = sampler
+        self.total_rows = int(rows)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.row_begin, self.row_end = row_range(self.total_rows, self.world, self.rank)
+        self.per = -(-self.total_rows // self.world)
+        dev = torch.device("cuda", sampler.device)
+        # this rank's tokens (row 0) and flags (row 1), padded to `per`
+        self.local = torch.zeros((2, self.per), dtype=torch.int32, device=dev)
+        self.gathered = torch.zeros((self.world, 2, self.per), dtype=torch.int32, device=dev)
+
+    @property
+    def rows(self) -> int:
+        return self.row_end - self.row_begin
+
+    def sample(self, logits_rows, hist_ids, hist_offsets, uniforms, params, stream=None) -> None:
+        """Asynchronous on `stream` (default: the current stream): samples this
+        rank's rows, then all-gathers every rank's tokens and flags."""
+        import torch
+        import torch.distributed as dist
+        if int(logits_rows.shape[0]) != self.rows:
+            raise ValueError(f"rank {self.rank} holds rows [{self.row_begin}, {self.row_end}), "
+                             f"got {int(logits_rows.shape[0])}")
+        ctx = torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+        with ctx:
+            cur = torch.cuda.current_stream(self.local.device)
+            if self.rows > 0:
+                self.sampler.sample_rows_device(logits_rows, hist_ids, hist_offsets, uniforms,
+                                                params, self.local[0, :self.rows],
+                                                self.local[1, :self.rows], None, cur)
+            if self.world > 1:
+                if dist.get_backend(self.group) == "nccl":
+                    dist.all_gather_into_tensor(self.gathered, self.local, group=self.group)
+                else:
+                    dist.all_gather(list(self.gathered.unbind(0)), self.local, group=self.group)
+            else:
+                self.gathered[0].copy_(self.local)
+
+    def tokens_flags(self):
+        """Every row's (tokens, flags) of the last call, in batch order, as
+        device tensors (synchronous only with the stream that sampled)."""
+        import torch
+        tok, fl = [], []
+        for r in range(self.world):
+            lo, hi = row_range(self.total_rows, self.world, r)
+            tok.append(self.gathered[r, 0, : hi - lo])
+            fl.append(self.gathered[r, 1, : hi - lo])
+        return torch.cat(tok), torch.cat(fl)
+
+
 class VocabShardedSampler:
     """Batched SampleNext over a vocabulary split in `vocab_range` shards, one per rank.
 

@@ -57,10 +57,15 @@ def test_zipf_ranked_shards(gpu_sampler, oracle, G):
 
 @pytest.mark.parametrize("G", [2, 4, 8])
 def test_vocab_sharded_workload(gpu_sampler, oracle, G):
-    wl = workloads.vocab_sharded(B=8, V=262144, H=2048, seed=22)
+    """The whole 128 x 262144 batch through the shard and merge kernels."""
+    from tests.gpu_util import parity_report
+    wl = workloads.vocab_sharded()
     st, sf, _ = assert_same_as_single(gpu_sampler, wl, G)
     ot, of, _ = run_oracle(oracle, wl, oracle.EXP_CR)
     assert_exact(st, sf, ot, of, f"vocab_sharded G={G}")
+    lt, lf, _ = run_oracle(oracle, wl, oracle.EXP_GLIBC)
+    rep = parity_report(st, sf, lt, lf)
+    assert rep["differ_unflagged"] == 0, rep
 
 
 def test_counts_and_raising_penalty(gpu_sampler, oracle):
