@@ -22,6 +22,7 @@
 #include "sampler_device.cuh"
 #include "topk_kernels.cuh"
 #include "topk_ldg_kernel.cuh"
+#include "topk_chunk_kernels.cuh"
 #include "vocab_merge.cuh"
 
 namespace {
@@ -71,6 +72,8 @@ struct NcbSampler {
   int max_smem_optin = 0;
   int max_dyn_smem = 0;  // dynamic shared memory a launch may request (opt-in minus static)
   int forced_splits = 0;  // NAVSAMPLER_SPLITS at creation (tuning only)
+  bool chunked = true;    // NAVSAMPLER_CHUNKED=0 at creation: top-k <= 64 on the one-CTA-per-row kernel
+  int ck_jmax = 0;        // chunks per row the chunked top-k scratch holds
   std::recursive_mutex mu;  // host-array entry points call the device ones under it
   void* scratch = nullptr;
   nvs::Scratch s{};
@@ -190,6 +193,10 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::nucleus_kernel<false>);
   set((const void*)nvs::fullvocab_kernel<true>);
   set((const void*)nvs::fullvocab_kernel<false>);
+  set((const void*)nvs::topk_chunk_finish_kernel<true, 4>);
+  set((const void*)nvs::topk_chunk_finish_kernel<false, 4>);
+  set((const void*)nvs::topk_chunk_finish_kernel<true, 8>);
+  set((const void*)nvs::topk_chunk_finish_kernel<false, 8>);
   set((const void*)nvs::fullvocab_fixup_kernel<true>);
   set((const void*)nvs::fullvocab_fixup_kernel<false>);
   set((const void*)nvs::filter_top_p_kernel);
@@ -276,6 +283,9 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   cudaDeviceGetAttribute(&h->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   h->max_dyn_smem = h->max_smem_optin - 4096;  // every kernel uses < 4 KiB of static smem
   if (const char* e = std::getenv("NAVSAMPLER_SPLITS")) h->forced_splits = std::atoi(e);
+  if (const char* e = std::getenv("NAVSAMPLER_CHUNKED")) h->chunked = std::atoi(e) != 0;
+  h->ck_jmax = nvs::ck_chunks(max_vocab);
+  if (h->ck_jmax > nvs::CK_MAX_CHUNKS) h->ck_jmax = nvs::CK_MAX_CHUNKS;
   h->max_ctas = max_rows > 2 * h->num_sms ? max_rows : 2 * h->num_sms;
   if (h->forced_splits > 0 && (size_t)max_rows * h->forced_splits > (size_t)h->max_ctas)
     h->max_ctas = max_rows * h->forced_splits;
@@ -302,6 +312,9 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   const size_t o_fx = carve((size_t)max_rows * sizeof(uint32_t));
   const size_t o_px = carve(4 * sizeof(uint32_t));
   const size_t o_st = carve(4 * sizeof(uint32_t));
+  const size_t ck_groups = (size_t)max_rows * h->ck_jmax * nvs::CK_WARPS;
+  const size_t o_ck = carve(ck_groups * nvs::CK_KEYS * sizeof(uint2));
+  const size_t o_cc = carve(ck_groups * sizeof(uint32_t));
   const nvs::FvLayout fl = nvs::fv_layout(max_rows, max_vocab);
   const size_t o_fv = carve(fl.total_bytes);
   if (cudaMalloc(&h->scratch, off) != cudaSuccess) {
@@ -320,6 +333,8 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->s.fixup = reinterpret_cast<uint32_t*>(b + o_fx);
   h->s.px_ticket = reinterpret_cast<uint32_t*>(b + o_px);
   h->s.stats = reinterpret_cast<uint32_t*>(b + o_st);
+  h->s.ck_keys = reinterpret_cast<uint2*>(b + o_ck);
+  h->s.ck_cnt = reinterpret_cast<uint32_t*>(b + o_cc);
   h->fv = nvs::fv_carve(b + o_fv, fl);
   // tickets/rowstate/error word must start at zero; the kernels restore zero
   if (!raise_smem_limits(h->max_smem_optin) || cudaMemset(h->scratch, 0, off) != cudaSuccess ||
@@ -400,6 +415,48 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   }
 
   const int K = prm->top_k < V ? prm->top_k : V;
+  // The chunked kernels: wide rows whose penalties can only lower a value,
+  // no probability output, and at most ~1.5 of the row's top K expected in
+  // one warp's 1024 values (a warp keeps >= 8 of them; a warp holding more
+  // sends the row to the exact fix-up).
+  const bool lowering = !(prm->repetition_penalty < 1.0f) && !(prm->frequency_penalty < 0.0f) &&
+                        !(prm->presence_penalty < 0.0f);
+  const int J = nvs::ck_chunks(V);
+  if (h->chunked && h->forced_splits == 0 && K < V && K <= nvs::TL_KMAX && !d_probs && lowering &&
+      V >= 8192 && J <= h->ck_jmax && 683LL * K <= (long long)V) {
+    a.bm_words = (V + 31) / 32 + 1;
+    const size_t smem = nvs::fk_smem_bytes(a.bm_words, a.h_cap);
+    if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c1{};
+    c1.gridDim = dim3(J, rows);
+    c1.blockDim = dim3(nvs::CK_THREADS);
+    c1.stream = stream;
+    c1.attrs = attr;
+    c1.numAttrs = 1;
+    if (cudaLaunchKernelEx(&c1, nvs::topk_chunk_kernel<false>, a) != cudaSuccess)
+      return NCB_ERROR_LAUNCH_FAILED;
+    cudaLaunchConfig_t c2{};
+    c2.gridDim = dim3(rows);
+    c2.blockDim = dim3(nvs::FK_THREADS);
+    c2.dynamicSmemBytes = smem;
+    c2.stream = stream;
+    c2.attrs = attr;
+    c2.numAttrs = 1;
+    const bool wide = J * nvs::CK_WARPS * nvs::CK_KEYS > 4 * nvs::FK_THREADS;
+    cudaError_t e;
+    if (counts)
+      e = wide ? cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<true, 8>, a, J)
+               : cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<true, 4>, a, J);
+    else
+      e = wide ? cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<false, 8>, a, J)
+               : cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<false, 4>, a, J);
+    if (e != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    // rows the finish could not prove (normally none)
+    return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, true, 8);
+  }
   if (K < V && K <= nvs::TL_KMAX) {
     int S = choose_splits_topk(rows, V, h->num_sms, h->forced_splits);
     a.seg_len = round_up((V + S - 1) / S, 4);

@@ -43,6 +43,9 @@ struct Scratch {
   uint32_t* px_ticket;  // [4] peer exchange: push CTAs, failed push waits, merge CTAs (zero
                         // between launches), epoch of the last call
   uint32_t* stats;      // [1] rows redone by the full-sort kernel (null: not counted)
+  uint2* ck_keys;       // chunked top-k: kept (raw value bits, column) per warp group,
+                        // [rows][chunks][8 warps][16]
+  uint32_t* ck_cnt;     // chunked top-k: count and state word per warp group
 };
 
 struct SampleArgs {
