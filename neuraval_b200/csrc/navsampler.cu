@@ -193,6 +193,7 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::nucleus_kernel<false>);
   set((const void*)nvs::fullvocab_kernel<true>);
   set((const void*)nvs::fullvocab_kernel<false>);
+  set((const void*)nvs::topk_chunk_kernel<false>);
   set((const void*)nvs::topk_chunk_finish_kernel<true, 4>);
   set((const void*)nvs::topk_chunk_finish_kernel<false, 4>);
   set((const void*)nvs::topk_chunk_finish_kernel<true, 8>);
@@ -430,13 +431,17 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const int nchunks = rows * J;
+    const size_t ring = nvs::cr_smem_bytes();
+    if ((int)ring > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
     cudaLaunchConfig_t c1{};
-    c1.gridDim = dim3(J, rows);
-    c1.blockDim = dim3(nvs::CK_THREADS);
+    c1.gridDim = dim3(nchunks < h->num_sms ? nchunks : h->num_sms);
+    c1.blockDim = dim3(nvs::CR_THREADS);
+    c1.dynamicSmemBytes = ring;
     c1.stream = stream;
     c1.attrs = attr;
     c1.numAttrs = 1;
-    if (cudaLaunchKernelEx(&c1, nvs::topk_chunk_kernel<false>, a) != cudaSuccess)
+    if (cudaLaunchKernelEx(&c1, nvs::topk_chunk_kernel<false>, a, J, nchunks) != cudaSuccess)
       return NCB_ERROR_LAUNCH_FAILED;
     cudaLaunchConfig_t c2{};
     c2.gridDim = dim3(rows);

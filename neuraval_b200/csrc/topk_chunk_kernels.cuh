@@ -70,105 +70,249 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return r;
 }
 
+// One warp group of 1024 values: lane l holds x[u] = the float4 at index
+// l + 32 u of the group (missing ones are -inf), also staged at sp (as
+// floats), whose first column is col0; plus one optional scalar xs at column
+// cs. Keeps every finite value >= the CK_RANK-th largest lane maximum (the
+// CK_RANK/2-th when that would keep more than CK_KEYS), writes them to keys[]
+// and returns the group word. All 32 lanes call; sp must stay valid until the
+// call returns.
+__device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const float* sp,
+                                             float xs, int cs, int col0, uint2* keys) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  float mu[CK_LOADS];
+#pragma unroll
+  for (int u = 0; u < CK_LOADS; ++u)
+    mu[u] = fmax_nan(fmax_nan(x[u].x, x[u].y), fmax_nan(x[u].z, x[u].w));
+  const float m = fmax_nan(fmax_nan(fmax_nan(fmax_nan(mu[0], mu[1]), fmax_nan(mu[2], mu[3])),
+                                    fmax_nan(fmax_nan(mu[4], mu[5]), fmax_nan(mu[6], mu[7]))),
+                           xs);
+  if (__any_sync(0xffffffffu, !(m < INFINITY))) return CK_W_NONFINITE;
+  // the largest lane maxima, popped CK_RANK times (order-preserving keys;
+  // equal maxima count once per lane)
+  uint32_t key = fkey(m);
+  uint32_t k4 = 0u, k8 = 0u;
+#pragma unroll
+  for (int r = 0; r < CK_RANK; ++r) {
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
+    const unsigned hit = __ballot_sync(0xffffffffu, key == mx);
+    if (lane == __ffs(hit) - 1) key = 0u;
+    if (r == CK_RANK / 2 - 1) k4 = mx;
+    k8 = mx;
+  }
+  for (int pass = 0; pass < 2; ++pass) {
+    const float t0 = kval(pass == 0 ? k8 : k4);
+    // kept: finite values >= t0 (t0 == -inf: fewer lanes than the rank hold a
+    // finite value, and every finite value is kept)
+    uint32_t mask = 0u;
+    const bool ks = xs >= t0 && xs > -INFINITY;
+    if (m >= t0 && m > -INFINITY) {
+#pragma unroll
+      for (int u = 0; u < CK_LOADS; ++u) {
+        if (mu[u] >= t0) {
+          mask |= (x[u].x >= t0 && x[u].x > -INFINITY ? 1u : 0u) << (4 * u);
+          mask |= (x[u].y >= t0 && x[u].y > -INFINITY ? 1u : 0u) << (4 * u + 1);
+          mask |= (x[u].z >= t0 && x[u].z > -INFINITY ? 1u : 0u) << (4 * u + 2);
+          mask |= (x[u].w >= t0 && x[u].w > -INFINITY ? 1u : 0u) << (4 * u + 3);
+        }
+      }
+    }
+    const int c = __popc(mask) + (ks ? 1 : 0);  // <= 33
+    const int total = __reduce_add_sync(0xffffffffu, (unsigned)c);
+    if (total > CK_KEYS) continue;
+    // exclusive prefix of c over the lanes, from the bits of c
+    int pos = 0;
+#pragma unroll
+    for (int b = 0; b < 6; ++b) pos += __popc(__ballot_sync(0xffffffffu, (c >> b) & 1) & lt) << b;
+    if (ks) keys[pos++] = make_uint2(__float_as_uint(xs), (uint32_t)cs);
+    while (mask) {
+      const int k = __ffs(mask) - 1;
+      mask &= mask - 1u;
+      const int f = 4 * (lane + 32 * (k >> 2)) + (k & 3);  // float index within the group
+      keys[pos++] = make_uint2(__float_as_uint(sp[f]), (uint32_t)(col0 + f));
+    }
+    return (uint32_t)total | (t0 == -INFINITY ? CK_W_ALLKEPT : 0u);
+  }
+  return CK_W_OVERFLOW | 0xFFFFu;
+}
+
+// Geometry of one row's columns [lo, hi) at base lrow (lrow[c] is column c):
+// the 16-byte aligned float4 body [a0, a0 + 4 n4) and the <= 3 + 3 scalars
+// around it.
+struct CkRow {
+  int a0, n4;
+};
+__device__ __forceinline__ CkRow ck_row(const float* lrow, int lo, int hi) {
+  const int head = (int)(((16u - ((uint32_t)(uintptr_t)(lrow + lo) & 15u)) & 15u) >> 2);
+  CkRow r;
+  r.a0 = min(lo + head, hi);
+  r.n4 = (hi - r.a0) >> 2;
+  return r;
+}
+
+// The stream: one CTA per SM, each over a contiguous share of the batch's
+// chunks (chunk t = row t / J, part t % J of the row's float4 body). A
+// producer warp keeps CR_STAGES 32 KiB bulk copies (cp.async.bulk, this GPU's
+// memory into this CTA's shared memory, mbarrier completion) in flight; three
+// teams of 8 consumer warps take the stages in turn (team t the stages i with
+// i % 3 == t), one 1024-value group per warp. Every wait is
+// bounded (about 2 s); a wait that gives up marks the chunk's groups so the
+// finish returns -1 for the row, and sets the error word.
+// mbarrier wait without a suspend-time hint, bounded by %globaltimer (about
+// 2 s); false when it gave up
+__device__ __forceinline__ bool cr_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 63) == 0) {
+      const uint64_t t = global_ns();
+      if (it == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) return false;
+    }
+  }
+}
+// global -> own shared memory bulk copy with an L2 evict-first policy: the
+// streamed logits must not push the kept values out of L2
+__device__ __forceinline__ void cr_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                        uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+constexpr int CR_STAGES = 6;
+constexpr int CR_TEAMS = 3;
+constexpr int CR_CONSUMERS = 8 * CR_TEAMS;
+constexpr int CR_THREADS = (CR_CONSUMERS + 1) * 32;
+constexpr uint32_t CK_W_TIMEOUT = 0x08000000u;  // a stage never arrived (group word)
+inline size_t cr_smem_bytes() { return (size_t)CR_STAGES * CK_F4 * 16 + 2 * CR_STAGES * 8; }
+
 template <bool kShard = false>
-__global__ void __launch_bounds__(CK_THREADS, 4) topk_chunk_kernel(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(CR_THREADS, 1) topk_chunk_kernel(const __grid_constant__ SampleArgs a, int J,
+                                                                   int nchunks) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  float4* stage = reinterpret_cast<float4*>(smem);                           // [STAGES][CK_F4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage + CR_STAGES * CK_F4);   // [STAGES]
+  uint64_t* empty = full + CR_STAGES;                                        // [STAGES]
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0c = (int)((long long)blockIdx.x * nchunks / gridDim.x);
+  const int t1c = (int)((long long)(blockIdx.x + 1) * nchunks / gridDim.x);
+  const int n = t1c - t0c;
+  const int lo = kShard ? a.col_lo : 0, hi = kShard ? a.col_hi : a.V;
+  if (tid == 0) {
+    for (int i = 0; i < CR_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CK_WARPS);  // the 8 warps of the team that read it
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  __syncthreads();
   // the logits may be written by the kernel before this one on the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // the finish kernel may be scheduled now; it waits for this grid to complete
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int j = blockIdx.x, J = gridDim.x, row = blockIdx.y;
-  const int lo = kShard ? a.col_lo : 0, hi = kShard ? a.col_hi : a.V;
-  // shard rows are addressed by global column: lrow[c] for c in [lo, hi)
-  const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * a.V;
-  // 16-byte aligned body [a0, a1) as float4, split evenly over the J chunks
-  const int head = (int)(((16u - ((uint32_t)(uintptr_t)(lrow + lo) & 15u)) & 15u) >> 2);
-  const int a0 = min(lo + head, hi);
-  const int n4 = (hi - a0) >> 2;
-  const int a1 = a0 + 4 * n4;
-  const int q0 = (int)((long long)j * n4 / J), q1 = (int)((long long)(j + 1) * n4 / J);
-  const float4* body = reinterpret_cast<const float4*>(lrow + a0);
-  float4 x[CK_LOADS];
-#pragma unroll
-  for (int u = 0; u < CK_LOADS; ++u) {
-    const int q = q0 + warp * 32 + lane + u * CK_THREADS;
-    x[u] = q < q1 ? __ldcs(body + q) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-  }
-  // the <= 3 head and <= 3 tail scalars: one extra value on lanes of chunk 0's warp 0
-  float xs = -INFINITY;
-  int cs = 0;
-  if (j == 0 && warp == 0) {
-    const int nh = a0 - lo, nt = hi - a1;
-    if (lane < nh + nt) {
-      cs = lane < nh ? lo + lane : a1 + (lane - nh);
-      xs = lrow[cs];
+  auto chunk = [&](int t, const float*& lrow, int& j, int& q0, int& q1, CkRow& g) {
+    const int row = t / J;
+    j = t - row * J;
+    lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * a.V;
+    g = ck_row(lrow, lo, hi);
+    q0 = (int)((long long)j * g.n4 / J);
+    q1 = (int)((long long)(j + 1) * g.n4 / J);
+    return row;
+  };
+  if (warp == CR_CONSUMERS) {
+    // producer: one elected lane issues the copies
+    if (lane == 0) {
+      uint64_t policy;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      for (int i = 0; i < n; ++i) {
+        const int st = i % CR_STAGES;
+        if (i >= CR_STAGES && !cr_wait(&empty[st], (uint32_t)(((i / CR_STAGES) - 1) & 1))) {
+          atomicOr(&s_abort, 1);
+          break;
+        }
+        if (*(volatile int*)&s_abort) break;
+        const float* lrow;
+        int j, q0, q1;
+        CkRow g;
+        chunk(t0c + i, lrow, j, q0, q1, g);
+        const uint32_t bytes = (uint32_t)(q1 - q0) * 16u;
+        mbar_arrive_expect_tx(&full[st], bytes);
+        if (bytes)
+          cr_copy(stage + (size_t)st * CK_F4, reinterpret_cast<const float4*>(lrow + g.a0) + q0,
+                  bytes, &full[st], policy);
+      }
     }
-  }
-  float m = xs;
-#pragma unroll
-  for (int u = 0; u < CK_LOADS; ++u)
-    m = fmax_nan(fmax_nan(fmax_nan(m, x[u].x), fmax_nan(x[u].y, x[u].z)), x[u].w);
-  const size_t g = ((size_t)row * J + j) * CK_WARPS + warp;
-  uint2* keys = a.s.ck_keys + g * CK_KEYS;
-  uint32_t word;
-  if (__any_sync(0xffffffffu, !(m < INFINITY))) {
-    word = CK_W_NONFINITE;
   } else {
-    // t0: the CK_RANK-th largest lane maximum (bitonic sort across lanes, descending)
-    float s = m;
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1)
-#pragma unroll
-      for (int jj = k >> 1; jj > 0; jj >>= 1) {
-        const float o = __shfl_xor_sync(0xffffffffu, s, jj);
-        const bool desc = (lane & k) == 0, lower = (lane & jj) == 0;
-        s = (desc == lower) ? fmaxf(s, o) : fminf(s, o);
+    const int team = warp / CK_WARPS, sub = warp % CK_WARPS;
+    for (int i = team; i < n; i += CR_TEAMS) {
+      const int st = i % CR_STAGES;
+      const float* lrow;
+      int j, q0, q1;
+      CkRow g;
+      const int row = chunk(t0c + i, lrow, j, q0, q1, g);
+      const size_t gidx = ((size_t)row * J + j) * CK_WARPS + sub;
+      const bool ok = cr_wait(&full[st], (uint32_t)((i / CR_STAGES) & 1));
+      if (!ok) {
+        if (lane == 0) {
+          a.s.ck_cnt[gidx] = CK_W_TIMEOUT;
+          atomicOr(&s_abort, 1);
+          atomicOr(a.s.error_word, 1u);
+        }
+        break;
       }
-    // kept: finite values >= t (t == -inf: fewer than CK_RANK lanes hold a
-    // finite value, and every finite value is kept)
-    auto count_kept = [&](float t, int& excl) {
-      auto keep = [&](float v) { return v >= t && v > -INFINITY; };
-      int c = keep(xs) ? 1 : 0;
-#pragma unroll
-      for (int u = 0; u < CK_LOADS; ++u)
-        c += (keep(x[u].x) ? 1 : 0) + (keep(x[u].y) ? 1 : 0) + (keep(x[u].z) ? 1 : 0) +
-             (keep(x[u].w) ? 1 : 0);
-      int incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t2 = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t2;
-      }
-      excl = incl - c;
-      return __shfl_sync(0xffffffffu, incl, 31);
-    };
-    float t0 = __shfl_sync(0xffffffffu, s, CK_RANK - 1);
-    int excl;
-    int total = count_kept(t0, excl);
-    if (total > CK_KEYS) {
-      // rare: more than CK_KEYS values reach the 8th lane maximum; the 4th
-      // keeps fewer (the finish still proves or redoes the row)
-      t0 = __shfl_sync(0xffffffffu, s, CK_RANK / 2 - 1);
-      total = count_kept(t0, excl);
-    }
-    if (total > CK_KEYS) {
-      word = CK_W_OVERFLOW | (uint32_t)min(total, 0xFFFF);
-    } else {
-      auto keep = [&](float v) { return v >= t0 && v > -INFINITY; };
-      int pos = excl;
-      if (keep(xs)) keys[pos++] = make_uint2(__float_as_uint(xs), (uint32_t)cs);
+      const int nq = q1 - q0;
+      const float4* sp = stage + (size_t)st * CK_F4 + sub * 256;
+      float4 x[CK_LOADS];
 #pragma unroll
       for (int u = 0; u < CK_LOADS; ++u) {
-        const int col = a0 + 4 * (q0 + warp * 32 + lane + u * CK_THREADS);
-        if (keep(x[u].x)) keys[pos++] = make_uint2(__float_as_uint(x[u].x), (uint32_t)col);
-        if (keep(x[u].y)) keys[pos++] = make_uint2(__float_as_uint(x[u].y), (uint32_t)(col + 1));
-        if (keep(x[u].z)) keys[pos++] = make_uint2(__float_as_uint(x[u].z), (uint32_t)(col + 2));
-        if (keep(x[u].w)) keys[pos++] = make_uint2(__float_as_uint(x[u].w), (uint32_t)(col + 3));
+        const int q = sub * 256 + lane + 32 * u;
+        x[u] = q < nq ? sp[lane + 32 * u] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       }
-      word = (uint32_t)total | (t0 == -INFINITY ? CK_W_ALLKEPT : 0u);
+      // the <= 3 head and <= 3 tail scalars of the row: group 0 of part 0
+      float xs = -INFINITY;
+      int cs = 0;
+      if (j == 0 && sub == 0) {
+        const int a1 = g.a0 + 4 * g.n4;
+        const int nh = g.a0 - lo, nt = hi - a1;
+        if (lane < nh + nt) {
+          cs = lane < nh ? lo + lane : a1 + (lane - nh);
+          xs = lrow[cs];
+        }
+      }
+      const uint32_t word = ck_group(x, reinterpret_cast<const float*>(sp), xs, cs,
+                                     g.a0 + 4 * (q0 + sub * 256), a.s.ck_keys + gidx * CK_KEYS);
+      if (lane == 0) a.s.ck_cnt[gidx] = word;
+      __syncwarp();
+      // the stage is read: release it to the producer
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
     }
   }
-  if (lane == 0) a.s.ck_cnt[g] = word;
+  // no bulk copy may still be landing in this CTA's shared memory when it exits
+  __syncthreads();
+  if (tid == 0 && s_abort) {
+    for (int st = 0; st < CR_STAGES && st < n; ++st) {
+      const int fills = (n - st + CR_STAGES - 1) / CR_STAGES;  // issued at most
+      cr_wait(&full[st], (uint32_t)((fills - 1) & 1));
+    }
+  }
+}
+
+// AdjustLogit for a value whose id is in the history (rare among the kept
+// values): one out-of-line copy instead of one per unrolled slot.
+__device__ __noinline__ float ck_adjust(const Penalty P, float raw, int col) {
+  return adjust(P, raw, col);
 }
 
 // float just below x (x finite): the largest float < x
@@ -185,7 +329,10 @@ inline size_t fk_smem_bytes(int bm_words, int h_cap) {
          + (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
 
-// FK_SLOTS key slots per thread: J * CK_WARPS * CK_KEYS <= FK_SLOTS * FK_THREADS.
+// One CTA per row. Slot s = tid + k * FK_THREADS of the row's G * CK_KEYS
+// kept-value slots is thread tid's k-th: group s / CK_KEYS, place s % CK_KEYS,
+// so the 16 slots of a group are 16 consecutive lanes (loads coalesce, group
+// reductions are half-warp shuffles). FK_SLOTS * FK_THREADS >= G * CK_KEYS.
 template <bool kCounts, int FK_SLOTS>
 __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const __grid_constant__ SampleArgs a, int J) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -196,12 +343,10 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   float* wS = w + 64;                                                  // [64]
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(wS + 64);
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
-  __shared__ int s_hn, s_nc, s_flags, s_c;
-  __shared__ uint32_t s_bkey, s_any;
-  __shared__ float s_L, s_u;
+  __shared__ int s_hn, s_nc;
+  __shared__ uint32_t s_bkey, s_any, s_lkey, s_vmax, s_slow[2];
+  __shared__ float s_u;
 
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x;
   const int V = a.V;
@@ -210,10 +355,32 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   // each group contributes its M largest exact values to the lower bound of
   // the K-th value (G * M >= K distinct elements)
   const int M = (K + G - 1) / G;
+  const int NT = G * M;
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
   const size_t gbase = (size_t)row * G;
 
-  // the row's kept values (every slot of every group; counts mask them below)
+  // Prologue on the call's inputs only (history, uniform): they were written
+  // before the chunk kernel started, which itself waited for them, so this
+  // part may overlap the chunk kernel's last CTAs. The chunk kernel's outputs
+  // are read after the wait below.
+  if (tid == 0) {
+    s_nc = 0;
+    s_bkey = 0u;
+    s_any = 0u;
+    s_lkey = 0xFFFFFFFFu;
+    s_vmax = 0u;
+    s_slow[0] = 0u;
+    s_slow[1] = 0u;
+    s_u = a.uniforms[row];
+  }
+  Penalty P;
+  const bool hist_ok =
+      setup_penalty_range<kCounts>(P, a, a.hoff[row], a.hoff[row + 1], 0, V, bitmap, hsorted, &s_hn);
+  const bool pen = P.rep || P.cnt;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   uint2 kv[FK_SLOTS];
   uint32_t gw[FK_SLOTS];
 #pragma unroll
@@ -227,37 +394,30 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
       gw[k] = 0u;
     }
   }
-  if (tid == 0) {
-    s_nc = 0;
-    s_flags = 0;
-    s_c = 0;
-    s_bkey = 0u;
-    s_any = 0u;
-    s_u = a.uniforms[row];
-  }
-  Penalty P;
-  const bool hist_ok =
-      setup_penalty_range<kCounts>(P, a, a.hoff[row], a.hoff[row + 1], 0, V, bitmap, hsorted, &s_hn);
 
-  // exact values of the kept slots; per group (16 consecutive threads) the
-  // largest exact value and the bound of what the group dropped
-  uint32_t any = 0u;  // bit 0 nonfinite group, bit 1 overflow, bit 2 exact +inf
+  // exact values of the kept slots; per group (16 consecutive lanes) its
+  // largest exact values and the bound of what the group dropped
+  uint32_t any = 0u;  // bit 0: nonfinite group or exact +inf, bit 1: overflow
+  uint32_t bk = 0u, vk = 0u;
   float v[FK_SLOTS];
 #pragma unroll
   for (int k = 0; k < FK_SLOTS; ++k) {
     const int s = tid + k * FK_THREADS, gi = s / CK_KEYS, e = s % CK_KEYS;
     const uint32_t word = gw[k];
-    const bool valid = gi < G && !(word & (CK_W_NONFINITE | CK_W_OVERFLOW)) &&
+    const bool valid = gi < G && !(word & (CK_W_NONFINITE | CK_W_OVERFLOW | CK_W_TIMEOUT)) &&
                        e < (int)(word & 0xFFFFu);
     if (gi < G && e == 0) {
-      if (word & CK_W_NONFINITE) any |= 1u;
+      if (word & (CK_W_NONFINITE | CK_W_TIMEOUT)) any |= 1u;
       if (word & CK_W_OVERFLOW) any |= 2u;
     }
     float ev = -INFINITY, raw = INFINITY;
     if (valid) {
       raw = __uint_as_float(kv[k].x);
-      ev = canon(__fmul_rn(adjust(P, raw, (int)kv[k].y), scale));
-      if (!(ev < INFINITY)) any |= 4u;  // scaled past the float range, as the reference's value
+      const int col = (int)kv[k].y;
+      float av = raw;
+      if (pen && ((bitmap[col >> 5] >> (col & 31)) & 1u)) av = ck_adjust(P, raw, col);
+      ev = canon(__fmul_rn(av, scale));
+      if (!(ev < INFINITY)) any |= 1u;  // scaled past the float range, as the reference's value
     }
     v[k] = ev;
     float gm = ev, tmin = raw;
@@ -278,24 +438,30 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
       for (int o = 8; o > 0; o >>= 1) g2 = fmaxf(g2, __shfl_xor_sync(0xffffffffu, g2, o));
     }
     if (gi < G && e == 0) {
-      if (M <= 2 && gi * M < FK_THREADS) {
+      if (M <= 2 && gi * M + M <= FK_THREADS) {
         gtop[gi * M] = gm;
         if (M == 2) gtop[gi * M + 1] = g2;
       }
+      if (gm > -INFINITY) vk = max(vk, fkey(gm));
       // a group that dropped values: they are < its smallest kept raw value
-      if (!(word & (CK_W_NONFINITE | CK_W_OVERFLOW | CK_W_ALLKEPT)) && tmin < INFINITY) {
-        const float b = canon(__fmul_rn(prev_float(tmin), scale));
-        atomicMax(&s_bkey, fkey(b));
-      }
+      if (!(word & (CK_W_NONFINITE | CK_W_OVERFLOW | CK_W_ALLKEPT | CK_W_TIMEOUT)) &&
+          tmin < INFINITY)
+        bk = max(bk, fkey(canon(__fmul_rn(prev_float(tmin), scale))));
     }
   }
   any = __reduce_or_sync(0xffffffffu, any);
-  if (lane == 0 && any) atomicOr(&s_any, any);
+  bk = __reduce_max_sync(0xffffffffu, bk);
+  vk = __reduce_max_sync(0xffffffffu, vk);
+  if (lane == 0) {
+    if (any) atomicOr(&s_any, any);
+    if (bk) atomicMax(&s_bkey, bk);
+    if (vk) atomicMax(&s_vmax, vk);
+  }
   __syncthreads();
   const uint32_t anyall = s_any;
   uint32_t state = 0u;
   if (!hist_ok) state = FLAG_BAD_HISTORY;
-  else if (anyall & 5u) state = FLAG_NONFINITE;
+  else if (anyall & 1u) state = FLAG_NONFINITE;
   if (state) {
     if (tid == 0) {
       a.tokens[row] = -1;
@@ -303,87 +469,91 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
     }
     return;
   }
-  const int NT = G * M;
-  bool fallback = (anyall & 2u) != 0u || M > 2 || NT > FK_THREADS;
-  // L: the K-th largest of the groups' M largest values (distinct elements,
-  // so a lower bound of the row's K-th largest value)
-  if (!fallback) {
-    if (tid < NT) {
-      const float x = gtop[tid];
-      int r = 0;
-      for (int h = 0; h < NT; ++h) {
-        const float y = gtop[h];
-        r += (y > x) || (y == x && h < tid);
-      }
-      if (r == K - 1) s_L = x;
+  if ((anyall & 2u) || M > 2 || NT > FK_THREADS || s_vmax == 0u) {
+    // the exact full-vocabulary kernel launched after this one redoes the row
+    if (tid == 0) a.s.fixup[row] = 1u;
+    return;
+  }
+  // L, a lower bound of the row's K-th largest value: warp w holds up to 32
+  // of the NT group values (distinct elements) and pops its q_w largest
+  // (q_w = ceil(K n_w / NT), so the q_w sum to >= K); L is the smallest of
+  // the warps' q_w-th largest values, so >= K elements are >= L.
+  if (warp < (NT + 31) / 32) {
+    const int nw = min(32, NT - 32 * warp);
+    const int q = (K * nw + NT - 1) / NT;
+    uint32_t key = lane < nw ? fkey(gtop[32 * warp + lane]) : 0u;
+    uint32_t qth = 0u;
+    for (int r = 0; r < q; ++r) {
+      qth = __reduce_max_sync(0xffffffffu, key);
+      const unsigned hit = __ballot_sync(0xffffffffu, key == qth);
+      if (lane == __ffs(hit) - 1) key = 0u;
     }
-    __syncthreads();
-    const float L = s_L;
-    if (!(L > -INFINITY)) {
-      fallback = true;  // fewer than K finite values: the exact path decides
-    } else {
-      // candidates: kept values >= L, as descending (value, id asc) keys
+    if (lane == 0) atomicMin(&s_lkey, qth);
+  }
+  __syncthreads();
+  if (s_lkey <= fkey(-INFINITY)) {  // fewer than K finite values: the exact path decides
+    if (tid == 0) a.s.fixup[row] = 1u;
+    return;
+  }
+  const float L = kval(s_lkey);
+  // candidates: kept values >= L, as descending (value, id asc) keys
 #pragma unroll
-      for (int k = 0; k < FK_SLOTS; ++k) {
-        const bool ok = v[k] >= L;
-        const unsigned b = __ballot_sync(0xffffffffu, ok);
-        if (b) {
-          const int leader = __ffs(b) - 1;
-          int base = 0;
-          if (lane == leader) base = atomicAdd(&s_nc, __popc(b));
-          base = __shfl_sync(0xffffffffu, base, leader);
-          const int slot = base + __popc(b & ((1u << lane) - 1u));
-          if (ok && slot < FK_CAND) cand[slot] = cand_key(v[k], (int)kv[k].y);
-        }
-      }
-      __syncthreads();
-      const int nc = s_nc;
-      if (nc > FK_CAND || nc < K) {
-        fallback = true;
-      } else {
-        // rank sort: the keys are distinct (ids are)
-        if (tid < nc) {
-          const uint64_t key = cand[tid];
-          int r = 0;
-          for (int h = 0; h < nc; ++h) r += cand[h] > key;
-          sorted[r] = key;
-        }
-        __syncthreads();
-        const uint64_t kth = sorted[K - 1];
-        const uint32_t tk = (uint32_t)(kth >> 32);
-        // every dropped value lies below the K-th value: it is the row's
-        if (s_bkey >= tk) {
-          fallback = true;
-        } else {
-          // the candidates: everything >= the K-th value (ties included)
-          if (tid >= K - 1 && tid < nc) {
-            const bool in = (uint32_t)(sorted[tid] >> 32) == tk;
-            const bool next_out = tid + 1 >= nc || (uint32_t)(sorted[tid + 1] >> 32) != tk;
-            if (in && next_out) s_c = tid + 1;
-          }
-          __syncthreads();
-          const int c = s_c;
-          if (c > 64) {
-            fallback = true;
-          } else {
-            const float vmax = cand_val(sorted[0]);
-            bool slow = false;
-            if (tid < c) w[tid] = exp_cr(__fsub_rn(cand_val(sorted[tid]), vmax), slow);
-            if (__any_sync(0xffffffffu, slow) && lane == 0) atomicOr(&s_flags, 1);
-            __syncthreads();
-            if (warp == 0) {
-              const uint64_t k0 = lane < c ? sorted[lane] : 0ull;
-              const uint64_t k1 = lane + 32 < c ? sorted[lane + 32] : 0ull;
-              finish_weights_warp(a, row, k0, k1, c, w, wS, s_flags != 0, s_u);
-            }
-            return;
-          }
-        }
-      }
+  for (int k = 0; k < FK_SLOTS; ++k) {
+    const bool ok = v[k] >= L;
+    const unsigned b = __ballot_sync(0xffffffffu, ok);
+    if (b) {
+      const int leader = __ffs(b) - 1;
+      int base = 0;
+      if (lane == leader) base = atomicAdd(&s_nc, __popc(b));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      const int slot = base + __popc(b & ((1u << lane) - 1u));
+      if (ok && slot < FK_CAND) cand[slot] = cand_key(v[k], (int)kv[k].y);
     }
   }
-  // the exact full-vocabulary kernel launched after this one redoes the row
-  if (fallback && tid == 0) a.s.fixup[row] = 1u;
+  __syncthreads();
+  const int nc = s_nc;
+  if (nc > FK_CAND || nc < K) {
+    if (tid == 0) a.s.fixup[row] = 1u;
+    return;
+  }
+  // rank sort (the keys are distinct: ids are) and the weights of the first
+  // 64 places, exp(v - max) with the row's largest value
+  const float vmax = kval(s_vmax);
+  if (tid < nc) {
+    const uint64_t key = cand[tid];
+    int r = 0;
+    int h = 0;
+    for (; h + 8 <= nc; h += 8) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) r += cand[h + d] > key;
+    }
+    for (; h < nc; ++h) r += cand[h] > key;
+    sorted[r] = key;
+    if (r < 64) {
+      bool slow = false;
+      w[r] = exp_cr(__fsub_rn(cand_val(key), vmax), slow);
+      if (slow) atomicOr(&s_slow[r >> 5], 1u << (r & 31));
+    }
+  }
+  __syncthreads();
+  // warp 0: the K-th value, the proof, the candidates (ties included) and the finish
+  if (warp == 0) {
+    const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);
+    const uint64_t k0 = lane < nc ? sorted[lane] : 0ull;
+    const uint64_t k1 = lane + 32 < nc ? sorted[lane + 32] : 0ull;
+    const bool over = nc > 64 && (uint32_t)(sorted[64] >> 32) == tk;  // > 64 candidates
+    // every dropped value lies below the K-th value: it is the row's
+    if (s_bkey >= tk || over) {
+      if (lane == 0) a.s.fixup[row] = 1u;
+    } else {
+      const unsigned b0 = __ballot_sync(0xffffffffu, k0 != 0ull && (uint32_t)(k0 >> 32) >= tk);
+      const unsigned b1 = __ballot_sync(0xffffffffu, k1 != 0ull && (uint32_t)(k1 >> 32) >= tk);
+      const int c = __popc(b0) + __popc(b1);
+      const bool any_slow = (s_slow[0] & b0) != 0u || (s_slow[1] & b1) != 0u;
+      finish_weights_warp(a, row, lane < c ? k0 : 0ull, lane + 32 < c ? k1 : 0ull, c, w, wS,
+                          any_slow, s_u);
+    }
+  }
 }
 
 }  // namespace nvs
