@@ -316,6 +316,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   const size_t ck_groups = (size_t)max_rows * h->ck_jmax * nvs::CK_WARPS;
   const size_t o_ck = carve(ck_groups * nvs::CK_KEYS * sizeof(uint2));
   const size_t o_cc = carve(ck_groups * sizeof(uint32_t));
+  const size_t o_ct = carve(ck_groups * sizeof(float));
   const nvs::FvLayout fl = nvs::fv_layout(max_rows, max_vocab);
   const size_t o_fv = carve(fl.total_bytes);
   if (cudaMalloc(&h->scratch, off) != cudaSuccess) {
@@ -336,6 +337,7 @@ NCB_API int ncb_sampler_create(int device, int max_rows, int max_vocab, int max_
   h->s.stats = reinterpret_cast<uint32_t*>(b + o_st);
   h->s.ck_keys = reinterpret_cast<uint2*>(b + o_ck);
   h->s.ck_cnt = reinterpret_cast<uint32_t*>(b + o_cc);
+  h->s.ck_cut = reinterpret_cast<float*>(b + o_ct);
   h->fv = nvs::fv_carve(b + o_fv, fl);
   // tickets/rowstate/error word must start at zero; the kernels restore zero
   if (!raise_smem_limits(h->max_smem_optin) || cudaMemset(h->scratch, 0, off) != cudaSuccess ||

@@ -75,10 +75,11 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 // floats), whose first column is col0; plus one optional scalar xs at column
 // cs. Keeps every finite value >= the CK_RANK-th largest lane maximum (the
 // CK_RANK/2-th when that would keep more than CK_KEYS), writes them to keys[]
-// and returns the group word. All 32 lanes call; sp must stay valid until the
-// call returns.
+// and the cutoff to *cut, and returns the group
+// word. All 32 lanes call; sp must stay valid until the call returns.
 __device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const float* sp,
-                                             float xs, int cs, int col0, uint2* keys) {
+                                             float xs, int cs, int col0, uint2* keys,
+                                             float* cut) {
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   float mu[CK_LOADS];
@@ -132,6 +133,7 @@ __device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const 
       const int f = 4 * (lane + 32 * (k >> 2)) + (k & 3);  // float index within the group
       keys[pos++] = make_uint2(__float_as_uint(sp[f]), (uint32_t)(col0 + f));
     }
+    *cut = t0;
     return (uint32_t)total | (t0 == -INFINITY ? CK_W_ALLKEPT : 0u);
   }
   return CK_W_OVERFLOW | 0xFFFFu;
@@ -291,9 +293,14 @@ __global__ void __launch_bounds__(CR_THREADS, 1) topk_chunk_kernel(const __grid_
           xs = lrow[cs];
         }
       }
+      float cut = -INFINITY;
       const uint32_t word = ck_group(x, reinterpret_cast<const float*>(sp), xs, cs,
-                                     g.a0 + 4 * (q0 + sub * 256), a.s.ck_keys + gidx * CK_KEYS);
-      if (lane == 0) a.s.ck_cnt[gidx] = word;
+                                     g.a0 + 4 * (q0 + sub * 256), a.s.ck_keys + gidx * CK_KEYS,
+                                     &cut);
+      if (lane == 0) {
+        a.s.ck_cnt[gidx] = word;
+        a.s.ck_cut[gidx] = cut;
+      }
       __syncwarp();
       // the stage is read: release it to the producer
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
@@ -383,15 +390,18 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
 
   uint2 kv[FK_SLOTS];
   uint32_t gw[FK_SLOTS];
+  float cut[FK_SLOTS];
 #pragma unroll
   for (int k = 0; k < FK_SLOTS; ++k) {
     const int s = tid + k * FK_THREADS, gi = s / CK_KEYS;
     if (gi < G) {
       kv[k] = __ldcg(a.s.ck_keys + (gbase + gi) * CK_KEYS + (s % CK_KEYS));
       gw[k] = __ldcg(a.s.ck_cnt + gbase + gi);
+      cut[k] = (s % CK_KEYS) == 0 ? __ldcg(a.s.ck_cut + gbase + gi) : 0.0f;
     } else {
       kv[k] = make_uint2(0u, 0u);
       gw[k] = 0u;
+      cut[k] = 0.0f;
     }
   }
 
@@ -410,9 +420,9 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
       if (word & (CK_W_NONFINITE | CK_W_TIMEOUT)) any |= 1u;
       if (word & CK_W_OVERFLOW) any |= 2u;
     }
-    float ev = -INFINITY, raw = INFINITY;
+    float ev = -INFINITY;
     if (valid) {
-      raw = __uint_as_float(kv[k].x);
+      const float raw = __uint_as_float(kv[k].x);
       const int col = (int)kv[k].y;
       float av = raw;
       if (pen && ((bitmap[col >> 5] >> (col & 31)) & 1u)) av = ck_adjust(P, raw, col);
@@ -420,20 +430,26 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
       if (!(ev < INFINITY)) any |= 1u;  // scaled past the float range, as the reference's value
     }
     v[k] = ev;
-    float gm = ev, tmin = raw;
-    int em = e;  // the slot of the group's largest value (lowest slot among equals)
+    if (valid) vk = max(vk, fkey(ev));
+    // the group's values for the lower bound: its largest exact value, and
+    // when M == 2 also its second largest
+    float gm = ev, g2 = -INFINITY;
+    if (M == 1) {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) {
-      const float og = __shfl_xor_sync(0xffffffffu, gm, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, em, o);
-      if (og > gm || (og == gm && oe < em)) {
-        gm = og;
-        em = oe;
+      for (int o = 8; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+    } else {
+      gm = ev;
+      int em = e;  // the slot of the group's largest value (lowest slot among equals)
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        const float og = __shfl_xor_sync(0xffffffffu, gm, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, em, o);
+        if (og > gm || (og == gm && oe < em)) {
+          gm = og;
+          em = oe;
+        }
       }
-      tmin = fminf(tmin, __shfl_xor_sync(0xffffffffu, tmin, o));
-    }
-    float g2 = e == em ? -INFINITY : ev;  // the second largest (M == 2)
-    if (M > 1) {
+      g2 = e == em ? -INFINITY : ev;
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) g2 = fmaxf(g2, __shfl_xor_sync(0xffffffffu, g2, o));
     }
@@ -442,11 +458,10 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
         gtop[gi * M] = gm;
         if (M == 2) gtop[gi * M + 1] = g2;
       }
-      if (gm > -INFINITY) vk = max(vk, fkey(gm));
-      // a group that dropped values: they are < its smallest kept raw value
+      // a group that dropped values: they are below its cutoff
       if (!(word & (CK_W_NONFINITE | CK_W_OVERFLOW | CK_W_ALLKEPT | CK_W_TIMEOUT)) &&
-          tmin < INFINITY)
-        bk = max(bk, fkey(canon(__fmul_rn(prev_float(tmin), scale))));
+          (word & 0xFFFFu) > 0u)
+        bk = max(bk, fkey(canon(__fmul_rn(prev_float(cut[k]), scale))));
     }
   }
   any = __reduce_or_sync(0xffffffffu, any);

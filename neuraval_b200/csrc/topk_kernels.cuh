@@ -46,6 +46,8 @@ struct Scratch {
   uint2* ck_keys;       // chunked top-k: kept (raw value bits, column) per warp group,
                         // [rows][chunks][8 warps][16]
   uint32_t* ck_cnt;     // chunked top-k: count and state word per warp group
+  float* ck_cut;        // chunked top-k: per warp group, the cutoff (kept values are >= it,
+                        // dropped ones below it)
 };
 
 struct SampleArgs {

@@ -226,32 +226,33 @@ __device__ __noinline__ void finish_keys_warp(const SampleArgs& a, int row, uint
 }
 
 // The rest of the finish once the weights w[i] = exp(v_i - max) of the m
-// sorted candidates are in shared memory (`S`: 64 floats of scratch, unused).
-// Every lane runs the same sequential fp32 sums (TokenSampler.cs:96-103) on
-// weights broadcast from registers and keeps S[lane] and S[lane + 32], so the
-// cutoff (:105-119) and draw (:125-132) searches are ballots on registers; the
-// boundary tests run on four lanes at once.
+// sorted candidates are in shared memory (`S`: 64 floats of shared scratch).
+// Lane 0 runs the sequential fp32 sums (TokenSampler.cs:96-103) into S; every
+// lane keeps S[lane] and S[lane + 32], so the cutoff (:105-119) and draw
+// (:125-132) searches are ballots on registers; the boundary tests run on
+// four lanes at once.
 __device__ __noinline__ void finish_weights_warp(const SampleArgs& a, int row, uint64_t k0,
                                                 uint64_t k1, int m, const float* __restrict__ w,
                                                 float* __restrict__ S, bool any_slow, float u) {
-  (void)S;
   const int lane = threadIdx.x & 31;
   uint64_t k[2] = {k0, k1};
   const float w_lo = lane < m ? w[lane] : 0.0f;
   const float w_hi = lane + 32 < m ? w[lane + 32] : 0.0f;
-  float s_lo = 0.0f, s_hi = 0.0f, total = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float wi = __shfl_sync(0xffffffffu, w_lo, i);
-    if (i < m) total = __fadd_rn(total, wi);
-    if (lane == i) s_lo = total;
+  // lane 0 runs the sequential sums from shared memory (the loads run ahead
+  // of the chain of adds), every lane then reads its S_i
+  if (lane == 0) {
+    float t = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < m; ++i) {
+      t = __fadd_rn(t, w[i]);
+      S[i] = t;
+    }
   }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float wi = __shfl_sync(0xffffffffu, w_hi, i);
-    if (32 + i < m) total = __fadd_rn(total, wi);
-    if (lane == i) s_hi = total;
-  }
+  __syncwarp();
+  const float s_lo = lane < m ? S[lane] : 0.0f;
+  const float s_hi = lane + 32 < m ? S[lane + 32] : 0.0f;
+  const float total = m > 0 ? S[m - 1] : 0.0f;
+  __syncwarp();
   // S[i] for a per-lane index i (every lane calls)
   auto S_at = [&](int i) -> float {
     const float lo = __shfl_sync(0xffffffffu, s_lo, i & 31);
