@@ -126,9 +126,9 @@ def measured_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes (read + write) per launch of the top-k kernel, from the committed
+    """DRAM bytes (read + write) per step of the top-k kernels, from the committed
     ncu summary of this workload (its `dram_bytes_per_launch:` line)."""
-    path = os.path.join(ROOT, "profiles", "topk_ldg_kernel_zipf_ranked_256x128256.md")
+    path = os.path.join(ROOT, "profiles", "topk_chunk_kernels_zipf_ranked_256x128256.md")
     try:
         with open(path) as fh:
             for line in fh:
@@ -262,6 +262,12 @@ def kernels_of(params, V):
     k = params.get("top_k", 0) or 0
     if params.get("greedy"):
         return "greedy_kernel", 1
+    lowering = (params.get("repetition_penalty", 1.0) >= 1.0 and
+                params.get("frequency_penalty", 0.0) >= 0.0 and
+                params.get("presence_penalty", 0.0) >= 0.0)
+    if 0 < k < V and k <= 64 and lowering and V >= 8192 and 683 * k <= V and V <= 262144:
+        return ("topk_chunk_kernel (stream) + topk_chunk_finish_kernel (+ the fix-up launch), "
+                "timed together"), 3
     if 0 < k < V and k <= 64:
         return "topk_ldg_kernel (+ its fix-up launch, timed together)", 2
     if 0 < k < V and k <= 1024:
