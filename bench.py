@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--extras", type=int, default=1,
                     help="headline only: 0 skips the extra measurements (replicas, "
                          "vocabulary shards, nucleus batch, one-row latency)")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="rows split over GPUs: every GPU's tokens and flags gathered to every "
+                         "GPU through peer memory by the library, or by an NCCL all-gather")
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
                     help="vocab_sharded: records exchanged by an NCCL all-gather, or through "
                          "peer memory by the shard kernel itself")
@@ -98,15 +101,21 @@ def nbuf_for(rows, V, least=NBUF):
     return max(least, -(-2 * L2_BYTES // max(1, rows * V * 4)))
 
 
-def rows_config(wl, world):
+GATHER_KERNEL = {"peer": " and row_gather_kernel (tokens stored into every GPU), per step",
+                 "nccl": " and the NCCL all-gather of the tokens, per step"}
+
+
+def rows_config(wl, world, gather="peer"):
     """The `config` of a rows-split line; identical in both arms of the bench."""
     from neuraval_b200 import sharding
     B, V = wl["logits"].shape
     H = int(wl["hist_offsets"][-1] // B)
     lo, hi = sharding.row_range(B, world, 0)
     nb = nbuf_for(hi - lo, V)
+    how = ("stored into every GPU over NVLink by the library" if gather == "peer" else
+           "all-gathered over NCCL")
     par = (f"{B} rows split over {world} GPUs (contiguous row ranges), token ids and flags "
-           "all-gathered over NCCL every step" if world > 1 else f"{B} rows on 1 GPU")
+           f"{how} every step" if world > 1 else f"{B} rows on 1 GPU")
     return {"workload": wl["name"], "B": B, "V": V, "history_per_row": H,
             **{k: v for k, v in wl["params"].items()},
             "uniforms": "one seeded u in [0,1) per row",
@@ -163,7 +172,7 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             self._sample()
-            time.sleep(0.005)
+            time.sleep(0.001)
 
     def _sample(self):
         try:
@@ -299,7 +308,7 @@ def run_reference(args, rank, world):
     dt = time.perf_counter() - t0
     value = B * args.steps / dt
     metric = METRIC if name == "zipf_ranked" else f"sampled rows/sec, {wl['name']}"
-    cfg = (rows_config(wl, world) if name != "vocab_sharded" else
+    cfg = (rows_config(wl, world, args.gather) if name != "vocab_sharded" else
            {"workload": wl["name"], "B": B, "V": wl["logits"].shape[1]})
     out = {"impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
@@ -351,9 +360,23 @@ def main():
 
 # ---- rows split over the GPUs ---------------------------------------------------
 
+def start_gate(dev, world):
+    """Queues work on the current stream ahead of a start event, without a host
+    synchronisation after it: an all-reduce of one word over the ranks (every
+    rank's timed region then starts within the all-reduce's own skew, not the
+    hosts') and a spin of about 50 microseconds, long enough for the host to
+    queue the timed launches behind the start event before it fires."""
+    import torch
+    if world > 1:
+        torch.distributed.all_reduce(torch.zeros(1, device=dev))
+    torch.cuda._sleep(100_000)
+
+
 def time_graph(fn, steps, dev, world, clocks=None):
     """`fn(i)` for i < steps captured once in a CUDA graph, one untimed replay,
-    then one replay between CUDA events on the current stream (ms)."""
+    then one replay between CUDA events on the current stream (ms). The clock
+    sampler's thread starts before the ranks line up, so that starting it
+    delays no rank's launches."""
     import torch
     cur = torch.cuda.current_stream(dev)
     graph = torch.cuda.CUDAGraph()
@@ -366,11 +389,12 @@ def time_graph(fn, steps, dev, world, clocks=None):
     torch.cuda.synchronize()
     graph.replay()
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with (clocks if clocks is not None else contextlib.nullcontext()):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        start_gate(dev, world)
         t0.record(cur)
         graph.replay()
         t1.record(cur)
@@ -383,7 +407,7 @@ class RowSplit:
     """One GPU's share of a row-split batch: its rows on the device (rotated
     copies), its sampler, and the all-gather of every GPU's tokens and flags."""
 
-    def __init__(self, wl, rank, world, dev, least_buffers=NBUF):
+    def __init__(self, wl, rank, world, dev, least_buffers=NBUF, gather="peer"):
         import torch
         from neuraval_b200 import native, sharding
         from neuraval_b200.sampler import CudaTokenSampler
@@ -408,9 +432,12 @@ class RowSplit:
                                                           dtype=np.int32)).to(dev)
         self.offs = torch.from_numpy((offs[lo: hi + 1] - offs[lo]).astype(np.int32)).to(dev)
         self.u = torch.from_numpy(np.ascontiguousarray(wl["uniforms"][lo:hi])).to(dev)
-        # world > 1: the library's row-split sampler (its rows, then one NCCL
-        # all-gather of every GPU's tokens and flags)
-        self.split = sharding.RowShardedSampler(self.sampler, B) if world > 1 else None
+        # world > 1: the library's row-split sampler (its rows, then every GPU's
+        # tokens and flags gathered to every GPU: peer stores or an NCCL all-gather)
+        self.split = None
+        if world > 1:
+            cls = sharding.PeerRowShardedSampler if gather == "peer" else sharding.RowShardedSampler
+            self.split = cls(self.sampler, B)
         self.local = torch.zeros((2, max(1, self.rows)), dtype=torch.int32, device=dev)
 
     def step(self, i):
@@ -435,18 +462,19 @@ class RowSplit:
         self.sampler.close()
 
 
-def run_split(wl, args, rank, world, dev, steps, clocks=None, least_buffers=NBUF):
+def run_split(wl, args, rank, world, dev, steps, clocks=None, least_buffers=NBUF, gather=None):
     """Times `steps` steps of the row-split batch (graph replay, max over ranks),
     then samples the unrotated batch once more for the parity check.
     Returns (ms for the steps, eager ms, tokens, flags, RowSplit)."""
     import torch
     from neuraval_b200 import sharding
-    rs = RowSplit(wl, rank, world, dev, least_buffers)
+    rs = RowSplit(wl, rank, world, dev, least_buffers, gather or args.gather)
     for i in range(max(3, args.warmup)):
         rs.step(i)
     torch.cuda.synchronize()
     cur = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start_gate(dev, world)
     e0.record(cur)
     for i in range(steps):
         rs.step(i)
@@ -486,6 +514,19 @@ def run_headline(args, rank, world, dev):
     if args.extras:
         extras["replicas"] = weak_replicas(args, rank, world, dev)
         torch.cuda.empty_cache()
+        if world > 1:
+            other = "nccl" if args.gather == "peer" else "peer"
+            o_ms, _, o_tok, o_fl, o_rs = run_split(wl, args, rank, world, dev, args.steps,
+                                                  gather=other)
+            o_rs.close()
+            del o_rs
+            torch.cuda.empty_cache()
+            if rank == 0:
+                extras[f"{other}_gather"] = {
+                    "value": B * args.steps / (o_ms / 1e3), "unit": UNIT,
+                    "ms_per_step": o_ms / args.steps,
+                    "kernel": kernels_of(wl["params"], V)[0] + GATHER_KERNEL[other],
+                    "parity": parity_of(wl, o_tok, o_fl)}
         extras["vocab_sharded"] = vocab_sharded_summary(args, rank, world, dev)
         torch.cuda.empty_cache()
         extras["high_entropy_nucleus"] = nucleus_split_summary(args, rank, world, dev)
@@ -508,12 +549,11 @@ def run_headline(args, rank, world, dev):
                "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
                "vs_baseline": None, "dtype": "fp32",
                "data": "synthetic (seeded generator, no dataset)",
-               "config": rows_config(wl, world),
+               "config": rows_config(wl, world, args.gather),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "peak_source": peak_kind,
                             "traffic": profiled_traffic() if world == 1 else None,
-                            "kernel": kernel + (" and the NCCL gather of the tokens, per step"
-                                                if world > 1 else ""),
+                            "kernel": kernel + (GATHER_KERNEL[args.gather] if world > 1 else ""),
                             "algorithmic_bytes_per_launch": bytes_per_launch,
                             "per_gpu_rows": rows_max},
                "gpu_launches": launches * args.steps,
@@ -651,7 +691,7 @@ def nucleus_split_summary(args, rank, world, dev):
         out = {"value": B * steps / (total_ms / 1e3), "unit": UNIT, "steps": steps,
                "ms_per_step": total_ms / steps, "hbm_frac": ach / peak,
                "kernel": kernels_of(wl["params"], V)[0],
-               "config": rows_config(wl, world), "parity": parity_of(wl, tok, fl)}
+               "config": rows_config(wl, world, args.gather), "parity": parity_of(wl, tok, fl)}
     return out
 
 
@@ -676,7 +716,8 @@ def run_rows_line(args, rank, world, dev, name):
            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": per_step_ms, "higher_is_better": True,
            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "fp32",
-           "data": "synthetic (seeded generator, no dataset)", "config": rows_config(wl, world),
+           "data": "synthetic (seeded generator, no dataset)",
+           "config": rows_config(wl, world, args.gather),
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                         "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
                         "kernel": kernel, "algorithmic_bytes_per_launch": bytes_per_launch},

@@ -257,6 +257,32 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* sampler, int rows, int
                                               const NcbSamplerParams* params, int32_t* d_tokens,
                                               uint32_t* d_flags, void* stream);
 
+/* ---- rows split over GPUs --------------------------------------------------
+ * No reference counterpart (the reference samples one row per call on one CPU
+ * thread). A batch split by rows over `ranks` GPUs, one process per GPU: each
+ * GPU samples its own rows, and every GPU gets every row's token and flags,
+ * gathered through peer memory instead of a collective. Each GPU's handle owns
+ * one gather area: ncb_row_gather_setup allocates it for rows_total rows and
+ * writes its CUDA IPC handle (ncb_peer_handle_bytes() bytes); the caller gives
+ * every handle all handles in rank order (ncb_row_gather_connect). Per call,
+ * on every GPU in the same order: ncb_sample_rows_gather_device samples this
+ * GPU's rows [row_begin, row_begin + rows) (arguments as ncb_sample_rows_device,
+ * rows <= max_rows), stores their tokens and flags into every GPU's area over
+ * NVLink, releases this call's flag there, waits (bounded, about 2 s) for every
+ * GPU's flag and writes all rows_total tokens (and flags, may be NULL) to
+ * d_tokens_all / d_flags_all. A wait that gives up returns every token as -1
+ * with NCB_FLAG_PEER_TIMEOUT. Asynchronous on `stream`. */
+NCB_API int ncb_row_gather_setup(NcbSampler* sampler, int ranks, int me, int rows_total,
+                                 void* handle_out);
+NCB_API int ncb_row_gather_connect(NcbSampler* sampler, const void* handles);
+NCB_API int ncb_sample_rows_gather_device(NcbSampler* sampler, const float* d_logits, int rows,
+                                          int vocab, int row_begin, const int32_t* d_hist,
+                                          const int32_t* d_hist_offsets,
+                                          const float* d_uniforms,
+                                          const NcbSamplerParams* params,
+                                          int32_t* d_tokens_all, uint32_t* d_flags_all,
+                                          void* stream);
+
 /* ---- row softmax ----------------------------------------------------------
  * ncb_cuda_softmax_rows_device (Neuraval.Cuda.Native/src/navcuda.cu:673-700)
  * with the arithmetic of its kernel (:616-671), output bits equal: row max,

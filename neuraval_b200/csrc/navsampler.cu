@@ -24,6 +24,7 @@
 #include "topk_ldg_kernel.cuh"
 #include "topk_chunk_kernels.cuh"
 #include "vocab_merge.cuh"
+#include "row_gather.cuh"
 
 namespace {
 
@@ -87,7 +88,9 @@ struct NcbSampler {
   uint32_t* h_flags_dev = nullptr;
   float* h_probs_dev = nullptr;
   size_t h_hist_cap = 0;
-  cudaStream_t host_stream = nullptr;
+  cudaStream_t host_stream = nullptr;  // sampling and the copies out
+  cudaStream_t copy_stream = nullptr;  // the copies in, slice by slice
+  cudaEvent_t slice_ev[8] = {};        // slice i of the logits is on the device
   // vocabulary shards exchanged through peer memory
   char* px_area = nullptr;  // this GPU's exchange area (records, flags, acks)
   int px_shards = 0, px_me = -1;
@@ -96,6 +99,13 @@ struct NcbSampler {
   char* px_base[nvs::PX_MAX] = {};  // every shard's area as mapped here
   bool px_imported[nvs::PX_MAX] = {};
   bool px_pushed = false;
+  // rows split over GPUs: tokens and flags gathered through peer memory
+  char* rg_area = nullptr;
+  int rg_ranks = 0, rg_me = -1, rg_rows_total = 0;
+  bool rg_connected = false;
+  nvs::RgLayout rg_layout{};
+  char* rg_base[nvs::PX_MAX] = {};
+  bool rg_imported[nvs::PX_MAX] = {};
 };
 
 namespace {
@@ -366,6 +376,17 @@ NCB_API int ncb_sampler_destroy(NcbSampler* h) {
         }
       cudaFree(h->px_area);
     }
+    if (h->rg_area) {
+      for (int s = 0; s < nvs::PX_MAX; ++s)
+        if (h->rg_imported[s]) cudaIpcCloseMemHandle(h->rg_base[s]);
+      std::lock_guard<std::mutex> lk(g_px_mu);
+      for (size_t i = 0; i < g_px_local.size(); ++i)
+        if (g_px_local[i].second == h->rg_area) {
+          g_px_local.erase(g_px_local.begin() + i);
+          break;
+        }
+      cudaFree(h->rg_area);
+    }
     cudaFree(h->scratch);
     cudaFree(h->h_logits_dev);
     cudaFree(h->h_hist_dev);
@@ -375,6 +396,9 @@ NCB_API int ncb_sampler_destroy(NcbSampler* h) {
     cudaFree(h->h_flags_dev);
     cudaFree(h->h_probs_dev);
     if (h->host_stream) cudaStreamDestroy(h->host_stream);
+    if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
+    for (cudaEvent_t e : h->slice_ev)
+      if (e) cudaEventDestroy(e);
   }
   delete h;
   return set_status(NCB_OK);
@@ -529,8 +553,11 @@ static bool ensure_staging(NcbSampler* h, size_t nh, bool probs) {
         cudaMalloc(&h->h_u_dev, (size_t)h->max_rows * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&h->h_tok_dev, (size_t)h->max_rows * sizeof(int32_t)) != cudaSuccess ||
         cudaMalloc(&h->h_flags_dev, (size_t)h->max_rows * sizeof(uint32_t)) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
       return false;
+    for (cudaEvent_t& e : h->slice_ev)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
   }
   if (nh > h->h_hist_cap) {
     cudaFree(h->h_hist_dev);
@@ -600,21 +627,48 @@ NCB_API int ncb_sample_rows(NcbSampler* h, const float* h_logits, int rows, int 
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   if (!ensure_staging(h, (size_t)nh, h_probs != nullptr)) return set_status(NCB_ERROR_ALLOC_FAILED);
-  cudaStream_t s = h->host_stream;
-  bool ok = cudaMemcpyAsync(h->h_logits_dev, h_logits, (size_t)rows * vocab * sizeof(float),
-                            cudaMemcpyHostToDevice, s) == cudaSuccess;
-  ok = ok && cudaMemcpyAsync(h->h_hoff_dev, h_hist_offsets, ((size_t)rows + 1) * sizeof(int32_t),
-                             cudaMemcpyHostToDevice, s) == cudaSuccess;
+  // The logits go in slices on the copy stream; slice i's sampling (on the
+  // sampling stream) waits for its own copy only, so sampling slice i overlaps
+  // copying slice i + 1 and the call ends one slice's sampling after the last
+  // copy. Rows are independent (TokenSampler.cs:10-30), so the slices' tokens
+  // equal the whole batch's.
+  cudaStream_t s = h->host_stream, cs = h->copy_stream;
+  const size_t row_bytes = (size_t)vocab * sizeof(float);
+  int slices = 1;
+  if ((size_t)rows * row_bytes >= ((size_t)16 << 20) && rows >= 32)
+    slices = rows / 16 < 8 ? rows / 16 : 8;
+  bool ok = cudaMemcpyAsync(h->h_hoff_dev, h_hist_offsets, ((size_t)rows + 1) * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, cs) == cudaSuccess;
   if (nh > 0)
     ok = ok && cudaMemcpyAsync(h->h_hist_dev, h_hist, (size_t)nh * sizeof(int32_t),
-                               cudaMemcpyHostToDevice, s) == cudaSuccess;
+                               cudaMemcpyHostToDevice, cs) == cudaSuccess;
   if (!params->greedy)
     ok = ok && cudaMemcpyAsync(h->h_u_dev, h_uniforms, (size_t)rows * sizeof(float),
-                               cudaMemcpyHostToDevice, s) == cudaSuccess;
-  if (!ok) return set_status(NCB_ERROR_COPY_FAILED);
-  st = launch_sample(h, h->h_logits_dev, rows, vocab, h->h_hist_dev, h->h_hoff_dev, h->h_u_dev,
-                     params, h->h_tok_dev, h->h_flags_dev, h_probs ? h->h_probs_dev : nullptr, s);
-  if (st != NCB_OK) return set_status(st);
+                               cudaMemcpyHostToDevice, cs) == cudaSuccess;
+  for (int i = 0; i < slices && ok; ++i) {
+    const int r0 = (int)((int64_t)rows * i / slices), r1 = (int)((int64_t)rows * (i + 1) / slices);
+    ok = cudaMemcpyAsync(h->h_logits_dev + (size_t)r0 * vocab, h_logits + (size_t)r0 * vocab,
+                         (size_t)(r1 - r0) * row_bytes, cudaMemcpyHostToDevice, cs) == cudaSuccess &&
+         cudaEventRecord(h->slice_ev[i], cs) == cudaSuccess;
+  }
+  if (!ok) {
+    cudaStreamSynchronize(cs);
+    return set_status(NCB_ERROR_COPY_FAILED);
+  }
+  for (int i = 0; i < slices; ++i) {
+    const int r0 = (int)((int64_t)rows * i / slices), r1 = (int)((int64_t)rows * (i + 1) / slices);
+    if (cudaStreamWaitEvent(s, h->slice_ev[i], 0) != cudaSuccess) st = NCB_ERROR_LAUNCH_FAILED;
+    if (st == NCB_OK)
+      st = launch_sample(h, h->h_logits_dev + (size_t)r0 * vocab, r1 - r0, vocab, h->h_hist_dev,
+                         h->h_hoff_dev + r0, h->h_u_dev + r0, params, h->h_tok_dev + r0,
+                         h->h_flags_dev + r0,
+                         h_probs ? h->h_probs_dev + (size_t)r0 * vocab : nullptr, s);
+    if (st != NCB_OK) {
+      cudaStreamSynchronize(cs);
+      cudaStreamSynchronize(s);
+      return set_status(st);
+    }
+  }
   ok = cudaMemcpyAsync(h_tokens, h->h_tok_dev, (size_t)rows * sizeof(int32_t),
                        cudaMemcpyDeviceToHost, s) == cudaSuccess;
   if (h_flags)
@@ -1240,6 +1294,125 @@ NCB_API int ncb_logits_filter_top_p(NcbSampler* h, float* h_probs, int rows, int
                                      [&](float* d, cudaStream_t s) {
     return ncb_logits_filter_top_p_device(h, d, rows, vocab, top_p, h->h_flags_dev, s);
   }));
+}
+
+
+// ---- rows split over GPUs, gathered through peer memory --------------------
+
+NCB_API int ncb_row_gather_setup(NcbSampler* h, int ranks, int me, int rows_total,
+                                 void* handle_out) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (ranks < 1 || ranks > nvs::PX_MAX || me < 0 || me >= ranks || rows_total <= 0 ||
+      !handle_out || h->rg_area)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  const nvs::RgLayout l = nvs::rg_layout(rows_total, h->max_rows);
+  void* area = nullptr;
+  if (cudaMalloc(&area, l.bytes) != cudaSuccess) return set_status(NCB_ERROR_ALLOC_FAILED);
+  cudaIpcMemHandle_t hd;
+  if (cudaMemset(area, 0, l.bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&hd, area) != cudaSuccess) {
+    cudaFree(area);
+    return set_status(NCB_ERROR_INIT_FAILED);
+  }
+  std::memcpy(handle_out, &hd, sizeof(hd));
+  {
+    std::lock_guard<std::mutex> lk2(g_px_mu);
+    std::array<char, sizeof(cudaIpcMemHandle_t)> key;
+    std::memcpy(key.data(), &hd, sizeof(hd));
+    g_px_local.emplace_back(key, static_cast<char*>(area));
+  }
+  h->rg_area = static_cast<char*>(area);
+  h->rg_ranks = ranks;
+  h->rg_me = me;
+  h->rg_rows_total = rows_total;
+  h->rg_layout = l;
+  h->rg_base[me] = h->rg_area;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_row_gather_connect(NcbSampler* h, const void* handles) {
+  if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!h->rg_area || h->rg_connected || !handles) return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  const char* hb = static_cast<const char*>(handles);
+  for (int s = 0; s < h->rg_ranks; ++s) {
+    if (s == h->rg_me) continue;
+    std::array<char, sizeof(cudaIpcMemHandle_t)> key;
+    std::memcpy(key.data(), hb + (size_t)s * sizeof(cudaIpcMemHandle_t), key.size());
+    char* local = nullptr;
+    {
+      std::lock_guard<std::mutex> lk2(g_px_mu);
+      for (const auto& e : g_px_local)
+        if (e.first == key) local = e.second;
+    }
+    if (local) {
+      h->rg_base[s] = local;
+      continue;
+    }
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, key.data(), sizeof(hd));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return set_status(NCB_ERROR_INIT_FAILED);
+    h->rg_base[s] = static_cast<char*>(p);
+    h->rg_imported[s] = true;
+  }
+  h->rg_connected = true;
+  return set_status(NCB_OK);
+}
+
+NCB_API int ncb_sample_rows_gather_device(NcbSampler* h, const float* d_logits, int rows,
+                                          int vocab, int row_begin, const int32_t* d_hist,
+                                          const int32_t* d_hist_offsets,
+                                          const float* d_uniforms,
+                                          const NcbSamplerParams* params,
+                                          int32_t* d_tokens_all, uint32_t* d_flags_all,
+                                          void* stream_) {
+  int st = validate_sample_args(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms,
+                                params, d_tokens_all);
+  if (st != NCB_OK) return set_status(st);
+  if (!h->rg_connected) return set_status(NCB_ERROR_NOT_INITIALIZED);
+  if (!d_tokens_all || row_begin < 0 || row_begin + rows > h->rg_rows_total)
+    return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  std::lock_guard<std::recursive_mutex> lk(h->mu);
+  DeviceGuard g(h->device);
+  if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int32_t* st_tok = reinterpret_cast<int32_t*>(h->rg_area + h->rg_layout.staging_off);
+  uint32_t* st_flg = reinterpret_cast<uint32_t*>(st_tok + h->max_rows);
+  if (rows > 0) {
+    st = launch_sample(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms, params, st_tok,
+                       st_flg, nullptr, stream);
+    if (st != NCB_OK) return set_status(st);
+  }
+  nvs::RgArgs ga{};
+  for (int s = 0; s < h->rg_ranks; ++s) ga.area[s] = h->rg_base[s];
+  ga.l = h->rg_layout;
+  ga.ranks = h->rg_ranks;
+  ga.me = h->rg_me;
+  ga.rows_total = h->rg_rows_total;
+  ga.max_rows = h->max_rows;
+  ga.row_begin = row_begin;
+  ga.rows = rows;
+  ga.out_tok = d_tokens_all;
+  ga.out_flg = d_flags_all;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(nvs::RG_THREADS);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, nvs::row_gather_kernel, ga) != cudaSuccess)
+    return set_status(NCB_ERROR_LAUNCH_FAILED);
+  return set_status(NCB_OK);
 }
 
 }  // extern "C"

@@ -100,10 +100,13 @@ __device__ __forceinline__ void shard_px_epilogue(const PxArgs& px, const uint32
       for (int s = 0; s < px.shards; ++s)
         if (s != px.me) px.dst[s][off + i] = v;
     }
-    __threadfence_system();  // the peer stores before this CTA's ticket
   }
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(px.ticket, 1u) == gridDim.x * gridDim.y - 1u;
+  if (tid == 0) {
+    // the barrier orders the CTA's peer stores before this one system fence
+    if (owner && s_go && px.shards > 1) __threadfence_system();
+    s_last = atomicAdd(px.ticket, 1u) == gridDim.x * gridDim.y - 1u;
+  }
   __syncthreads();
   if (s_last && tid == 0) {
     __threadfence_system();

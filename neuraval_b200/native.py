@@ -79,6 +79,10 @@ SIGNATURES = {
                                               ctypes.POINTER(NcbSamplerParams), _P]),
     "ncb_vocab_shard_merge_peer_device": (_I, [_P, _I, _I, _P, ctypes.POINTER(NcbSamplerParams),
                                                _P, _P, _P]),
+    "ncb_row_gather_setup": (_I, [_P, _I, _I, _I, _P]),
+    "ncb_row_gather_connect": (_I, [_P, _P]),
+    "ncb_sample_rows_gather_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P,
+                                           ctypes.POINTER(NcbSamplerParams), _P, _P, _P]),
     "ncb_softmax_rows_device": (_I, [_P, _P, _I, _I, _P]),
     "ncb_logits_repetition_penalty": (_I, [_P, _P, _I, _I, _P, _P, _F]),
     "ncb_logits_frequency_presence_penalty": (_I, [_P, _P, _I, _I, _P, _P, _F, _F]),

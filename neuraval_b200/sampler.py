@@ -144,6 +144,37 @@ class CudaTokenSampler:
             self._h, int(rows), int(vocab), _ptr(uniforms), ctypes.byref(params), _ptr(tokens),
             _ptr(flags), _stream_ptr(stream)), "ncb_vocab_shard_merge_peer_device")
 
+    # rows split over GPUs, gathered through peer memory
+    def row_gather_setup(self, ranks: int, me: int, rows_total: int) -> bytes:
+        """Allocates this GPU's gather area; returns its IPC handle."""
+        n = int(self._lib.ncb_peer_handle_bytes())
+        buf = ctypes.create_string_buffer(n)
+        check(self._lib.ncb_row_gather_setup(self._h, int(ranks), int(me), int(rows_total), buf),
+              "ncb_row_gather_setup")
+        self._rg_rows_total = int(rows_total)
+        return buf.raw
+
+    def row_gather_connect(self, handles: bytes) -> None:
+        """`handles`: every rank's handle, concatenated in rank order."""
+        buf = ctypes.create_string_buffer(handles, len(handles))
+        check(self._lib.ncb_row_gather_connect(self._h, buf), "ncb_row_gather_connect")
+
+    def sample_rows_gather_device(self, logits, row_begin: int, hist_ids, hist_offsets, uniforms,
+                                  params: NcbSamplerParams, tokens_all, flags_all=None,
+                                  stream=None) -> None:
+        """This GPU's rows [row_begin, row_begin + rows); every row's token and
+        flags into tokens_all / flags_all (rows_total each)."""
+        rows, vocab = int(logits.shape[0]), int(logits.shape[1])
+        total = getattr(self, "_rg_rows_total", 0)
+        for name, t in (("tokens_all", tokens_all), ("flags_all", flags_all)):
+            if t is not None and (t.numel() < total or t.element_size() != 4
+                                  or not t.is_contiguous()):
+                raise ValueError(f"{name} must be {total} contiguous 32-bit words")
+        check(self._lib.ncb_sample_rows_gather_device(
+            self._h, _ptr(logits), rows, vocab, int(row_begin), _ptr(hist_ids),
+            _ptr(hist_offsets), _ptr(uniforms), ctypes.byref(params), _ptr(tokens_all),
+            _ptr(flags_all), _stream_ptr(stream)), "ncb_sample_rows_gather_device")
+
     # ---- LogitsProcessor (in place, device tensors) ----------------------
     def repetition_penalty_(self, logits, hist_ids, hist_offsets, penalty, stream=None):
         check(self._lib.ncb_logits_repetition_penalty_device(

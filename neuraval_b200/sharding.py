@@ -2,8 +2,9 @@
 
 TokenSampler.SampleNext (Neuraval/Generation/TokenSampler.cs:10-143) treats
 every row on its own, so a batch splits two ways:
-  - by rows (`row_range`): each GPU samples its rows with the single-GPU entry
-    point; no data crosses GPUs (an optional all-gather of the B int32 tokens);
+  - by rows (`row_range`, `RowShardedSampler`, `PeerRowShardedSampler`): each
+    GPU samples its rows with the single-GPU kernels; every GPU then gets all
+    rows' tokens and flags, by an NCCL all-gather or through peer memory;
   - by vocabulary (`vocab_range`, `VocabShardedSampler`): each GPU holds its
     columns of every row (a tensor-parallel LM head), reduces them to one
     fixed-size record per row, the records of all GPUs are all-gathered in
@@ -128,6 +129,42 @@ class RowShardedSampler:
             tok.append(self.gathered[r, 0, : hi - lo])
             fl.append(self.gathered[r, 1, : hi - lo])
         return torch.cat(tok), torch.cat(fl)
+
+
+class PeerRowShardedSampler(RowShardedSampler):
+    """RowShardedSampler whose gather is done by the library through peer memory
+    (each GPU stores its rows' tokens and flags into every GPU's gather area
+    over NVLink and releases a per-call flag there) instead of an NCCL
+    all-gather. The process group is used once, to exchange the areas' IPC
+    handles."""
+
+    def __init__(self, sampler, rows: int, group=None):
+        import torch
+        import torch.distributed as dist
+        super().__init__(sampler, rows, group)
+        mine = sampler.row_gather_setup(self.world, self.rank, self.total_rows)
+        n = len(mine)
+        local = torch.tensor(list(mine), dtype=torch.uint8)
+        if dist.is_initialized() and dist.get_backend(group) == "nccl":
+            local = local.cuda(sampler.device)
+        everyone = gather_records(local.view(1, n), group)  # [world, 1, n], rank order
+        sampler.row_gather_connect(bytes(everyone.view(-1).cpu().tolist()))
+        dev = self.local.device
+        self.tokens_all = torch.zeros(self.total_rows, dtype=torch.int32, device=dev)
+        self.flags_all = torch.zeros(self.total_rows, dtype=torch.int32, device=dev)
+
+    def sample(self, logits_rows, hist_ids, hist_offsets, uniforms, params, stream=None) -> None:
+        import torch
+        if int(logits_rows.shape[0]) != self.rows:
+            raise ValueError(f"rank {self.rank} holds rows [{self.row_begin}, {self.row_end}), "
+                             f"got {int(logits_rows.shape[0])}")
+        cur = stream if stream is not None else torch.cuda.current_stream(self.local.device)
+        self.sampler.sample_rows_gather_device(logits_rows, self.row_begin, hist_ids, hist_offsets,
+                                               uniforms, params, self.tokens_all, self.flags_all,
+                                               cur)
+
+    def tokens_flags(self):
+        return self.tokens_all, self.flags_all
 
 
 class VocabShardedSampler:

@@ -1,6 +1,7 @@
 """Sampling over two real GPUs, one process per GPU, NCCL over NVLink: the
-headline batch split by rows (each GPU samples its rows, one all-gather of the
-tokens and flags) and the 128 x 262144 batch split by vocabulary (shard
+headline batch split by rows (each GPU samples its rows; the tokens and flags
+gathered by one NCCL all-gather, or stored into every GPU over NVLink by the
+library's row_gather_kernel) and the 128 x 262144 batch split by vocabulary (shard
 records all-gathered, merged on every GPU). Every rank gets all rows' tokens;
 rank 0 checks them against the oracle bit for bit (correctly rounded exp) and
 against libm expf (rows may differ only where a boundary or tie flag is set).
@@ -33,6 +34,39 @@ def _check(wl, tok, fl):
     assert rep["differ_unflagged"] == 0, rep
 
 
+def _rows_peer(rank, world, dev):
+    """The row split with the library's peer-memory gather: three calls, the
+    uniforms changed between them, so a copy left from an earlier call (the
+    gather alternates between two copies) would show."""
+    import torch
+    from neuraval_b200 import native, sharding, workloads
+    from neuraval_b200.sampler import CudaTokenSampler
+    wl = workloads.zipf_ranked()
+    B, V = wl["logits"].shape
+    H = int(wl["hist_offsets"][-1] // B)
+    lo, hi = sharding.row_range(B, world, rank)
+    offs = np.asarray(wl["hist_offsets"], np.int64)
+    variants = [wl, dict(wl, uniforms=np.ascontiguousarray(np.roll(wl["uniforms"], 37)),
+                         name=wl["name"] + " (uniforms rolled)"), wl]
+    with CudaTokenSampler(rank, max_rows=hi - lo, max_vocab=V, max_history=H) as s:
+        rs = sharding.PeerRowShardedSampler(s, B)
+        logits = torch.from_numpy(np.ascontiguousarray(wl["logits"][lo:hi])).to(dev)
+        hist = torch.from_numpy(np.ascontiguousarray(wl["hist_ids"][offs[lo]:offs[hi]])).to(dev)
+        ho = torch.from_numpy((offs[lo:hi + 1] - offs[lo]).astype(np.int32)).to(dev)
+        p = native.make_params(**wl["params"])
+        for v in variants:
+            u = torch.from_numpy(np.ascontiguousarray(v["uniforms"][lo:hi])).to(dev)
+            rs.sample(logits, hist, ho, u, p)
+            tok, fl = rs.tokens_flags()
+            torch.cuda.synchronize()
+            tok = tok.cpu().numpy()
+            fl = fl.cpu().numpy().astype(np.uint32)
+            assert not np.any(fl & native.FLAG_PEER_TIMEOUT), rank
+            if rank == 0:
+                _check(v, tok, fl)
+        torch.cuda.synchronize()
+
+
 def _rank_main(rank, world, port, case):
     import torch
     import torch.distributed as dist
@@ -44,7 +78,9 @@ def _rank_main(rank, world, port, case):
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
-        if case == "rows":
+        if case == "rows_peer":
+            _rows_peer(rank, world, dev)
+        elif case == "rows":
             wl = workloads.zipf_ranked()
             B, V = wl["logits"].shape
             H = int(wl["hist_offsets"][-1] // B)
@@ -94,7 +130,7 @@ def _rank_main(rank, world, port, case):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["rows", "vocab"])
+@pytest.mark.parametrize("case", ["rows", "rows_peer", "vocab"])
 def test_two_gpus_nccl(case):
     import torch
     import torch.multiprocessing as mp

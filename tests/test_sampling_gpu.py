@@ -67,6 +67,30 @@ def test_zipf_ranked_full_size(gpu_sampler, oracle):
     print("zipf_ranked parity", rep)
 
 
+@pytest.mark.parametrize("name", ["zipf_ranked", "high_entropy_nucleus"])
+def test_host_arrays_sliced_copies(gpu_sampler, oracle, name):
+    """ncb_sample_rows with host arrays: batches of 16 MiB and more go in
+    slices (each sliced call samples its rows while the next slice copies);
+    the tokens, flags and probabilities equal the oracle's for the whole
+    batch."""
+    wl = getattr(workloads, name)()
+    if name == "high_entropy_nucleus":
+        sel = slice(0, 96)  # 96 x 151936 rows: 58 MB, six slices
+        offs = np.asarray(wl["hist_offsets"], np.int64)
+        wl = dict(wl, logits=np.ascontiguousarray(wl["logits"][sel]),
+                  hist_ids=np.ascontiguousarray(wl["hist_ids"][offs[0]:offs[96]]),
+                  hist_offsets=offs[:97].copy(), uniforms=np.ascontiguousarray(wl["uniforms"][sel]))
+    p = native.make_params(**wl["params"])
+    want_probs = name == "zipf_ranked"
+    gt, gf, gp = gpu_sampler.sample_rows(wl["logits"], wl["hist_ids"],
+                                         np.asarray(wl["hist_offsets"], np.int32), wl["uniforms"],
+                                         p, want_probs=want_probs)
+    ot, of, op = run_oracle(oracle, wl, oracle.EXP_CR, want_probs=want_probs)
+    assert_exact(gt, gf.astype(np.uint32), ot, of, name + " host arrays")
+    if want_probs:
+        assert np.array_equal(gp, op)
+
+
 @pytest.mark.parametrize("mantissa_bits", [7, 3])
 def test_quantised_logits_with_ties(gpu_sampler, oracle, mantissa_bits):
     # logits of a bf16 model (7 mantissa bits) and coarser: many exactly equal
