@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="rows split over GPUs: every GPU's tokens and flags gathered to every "
                          "GPU through peer memory by the library, or by an NCCL all-gather")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="vocab_sharded: records exchanged by an NCCL all-gather, or through "
                          "peer memory by the shard kernel itself")
     ap.add_argument("--workload", default="zipf_ranked",
@@ -556,7 +556,8 @@ def run_headline(args, rank, world, dev):
                             "kernel": kernel + (GATHER_KERNEL[args.gather] if world > 1 else ""),
                             "algorithmic_bytes_per_launch": bytes_per_launch,
                             "per_gpu_rows": rows_max},
-               "gpu_launches": launches * args.steps,
+               "gpu_launches": (launches + (1 if world > 1 and args.gather == "peer" else 0))
+                               * args.steps,
                "eager_value": B * args.steps / (eager_ms / 1e3),
                "timing": "CUDA events around one replay of a CUDA graph holding the K steps "
                          "(the token all-gather included); max over ranks",
@@ -735,7 +736,7 @@ def run_rows_line(args, rank, world, dev, name):
 
 # ---- vocabulary split over the GPUs ----------------------------------------------
 
-def vocab_sharded_measure(args, rank, world, dev, clocks=None):
+def vocab_sharded_measure(args, rank, world, dev, clocks=None, exchange=None):
     """The 128 x 262144 batch (top-k 64) with its vocabulary split over the ranks:
     per step, the shard candidate kernel, one NCCL all-gather of the records and
     the merge kernel on every rank. Total work is fixed (strong scaling). The
@@ -767,7 +768,8 @@ def vocab_sharded_measure(args, rank, world, dev, clocks=None):
     words = sampler.shard_record_bytes // 4
     local = torch.zeros((B, words), dtype=torch.int32, device=dev)
     gathered = torch.zeros((world, B, words), dtype=torch.int32, device=dev)
-    peer = sharding.PeerVocabShardedSampler(sampler, V) if args.exchange == "peer" else None
+    exchange = exchange or args.exchange
+    peer = sharding.PeerVocabShardedSampler(sampler, V) if exchange == "peer" else None
 
     def candidates(i):
         sampler.shard_candidates_device(bufs[i % nbuf], V, lo, hist, offs, params, local,
@@ -831,10 +833,22 @@ def vocab_sharded_measure(args, rank, world, dev, clocks=None):
 
 def vocab_sharded_summary(args, rank, world, dev):
     r = vocab_sharded_measure(args, rank, world, dev)
+    other = None
+    if world > 1:
+        import torch
+        torch.cuda.empty_cache()
+        o = vocab_sharded_measure(args, rank, world, dev,
+                                  exchange="nccl" if args.exchange == "peer" else "peer")
+        if rank == 0:
+            other = {"ms_per_step": o["total_ms"] / args.steps,
+                     "parts_us_per_step": {"candidates": o["parts"][0] / args.steps * 1e3,
+                                           "exchange": o["parts"][1] / args.steps * 1e3,
+                                           "merge": o["parts"][2] / args.steps * 1e3},
+                     "tokens_match_single_gpu": o["ok"]}
     if rank != 0:
         return None
     s = args.steps
-    return {"value": r["B"] * s / (r["total_ms"] / 1e3), "unit": UNIT,
+    out = {"value": r["B"] * s / (r["total_ms"] / 1e3), "unit": UNIT,
             "ms_per_step": r["total_ms"] / s, "n_gpus": world, "shard_columns": r["width"],
             "parts_us_per_step": {"candidates": r["parts"][0] / s * 1e3,
                                   "exchange": r["parts"][1] / s * 1e3,
@@ -845,6 +859,9 @@ def vocab_sharded_summary(args, rank, world, dev):
             "parity": parity_of(r["wl"], r["tokens"], r["flags"]),
             "config": {"workload": r["wl"]["name"], "B": r["B"], "V": r["V"],
                        "parallelism": f"vocabulary split over {world} GPU(s)"}}
+    if other is not None:
+        out["nccl_exchange" if args.exchange == "peer" else "peer_exchange"] = other
+    return out
 
 
 def run_vocab_sharded(args, rank, world, dev):

@@ -69,6 +69,18 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
+// the three-input form (sm_100)
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// all ones when a >= b, else zero (set.ge.u32.f32; false when either is NaN)
+__device__ __forceinline__ uint32_t fge_mask(float a, float b) {
+  uint32_t d;
+  asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(d) : "f"(a), "f"(b));
+  return d;
+}
 
 // One warp group of 1024 values: lane l holds x[u] = the float4 at index
 // l + 32 u of the group (missing ones are -inf), also staged at sp (as
@@ -80,15 +92,18 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 __device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const float* sp,
                                              float xs, int cs, int col0, uint2* keys,
                                              float* cut) {
+  static_assert(CK_LOADS == 8, "the maximum tree below reads eight float4");
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
-  float mu[CK_LOADS];
+  // lane maximum of the 32 values and xs: a tree of three-input maxima
+  float t[11];
 #pragma unroll
-  for (int u = 0; u < CK_LOADS; ++u)
-    mu[u] = fmax_nan(fmax_nan(x[u].x, x[u].y), fmax_nan(x[u].z, x[u].w));
-  const float m = fmax_nan(fmax_nan(fmax_nan(fmax_nan(mu[0], mu[1]), fmax_nan(mu[2], mu[3])),
-                                    fmax_nan(fmax_nan(mu[4], mu[5]), fmax_nan(mu[6], mu[7]))),
-                           xs);
+  for (int u = 0; u < 8; ++u) t[u] = fmax3_nan(x[u].x, x[u].y, x[u].z);
+  t[8] = fmax3_nan(x[0].w, x[1].w, x[2].w);
+  t[9] = fmax3_nan(x[3].w, x[4].w, x[5].w);
+  t[10] = fmax3_nan(x[6].w, x[7].w, xs);
+  const float m = fmax3_nan(fmax3_nan(t[0], t[1], t[2]), fmax3_nan(t[3], t[4], t[5]),
+                            fmax3_nan(fmax3_nan(t[6], t[7], t[8]), t[9], t[10]));
   if (__any_sync(0xffffffffu, !(m < INFINITY))) return CK_W_NONFINITE;
   // the largest lane maxima, popped CK_RANK times (order-preserving keys;
   // equal maxima count once per lane)
@@ -105,27 +120,25 @@ __device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const 
   for (int pass = 0; pass < 2; ++pass) {
     const float t0 = kval(pass == 0 ? k8 : k4);
     // kept: finite values >= t0 (t0 == -inf: fewer lanes than the rank hold a
-    // finite value, and every finite value is kept)
+    // finite value, and every finite value is kept); no value here is NaN or
+    // +inf, so "finite and >= t0" is ">= max(t0, lowest float)"
+    const float tf = fmaxf(t0, -3.40282347e+38f);
     uint32_t mask = 0u;
-    const bool ks = xs >= t0 && xs > -INFINITY;
-    if (m >= t0 && m > -INFINITY) {
 #pragma unroll
-      for (int u = 0; u < CK_LOADS; ++u) {
-        if (mu[u] >= t0) {
-          mask |= (x[u].x >= t0 && x[u].x > -INFINITY ? 1u : 0u) << (4 * u);
-          mask |= (x[u].y >= t0 && x[u].y > -INFINITY ? 1u : 0u) << (4 * u + 1);
-          mask |= (x[u].z >= t0 && x[u].z > -INFINITY ? 1u : 0u) << (4 * u + 2);
-          mask |= (x[u].w >= t0 && x[u].w > -INFINITY ? 1u : 0u) << (4 * u + 3);
-        }
-      }
+    for (int u = 0; u < 8; ++u) {
+      mask |= fge_mask(x[u].x, tf) & (1u << (4 * u));
+      mask |= fge_mask(x[u].y, tf) & (1u << (4 * u + 1));
+      mask |= fge_mask(x[u].z, tf) & (1u << (4 * u + 2));
+      mask |= fge_mask(x[u].w, tf) & (1u << (4 * u + 3));
     }
+    const bool ks = xs >= tf;
     const int c = __popc(mask) + (ks ? 1 : 0);  // <= 33
     const int total = __reduce_add_sync(0xffffffffu, (unsigned)c);
     if (total > CK_KEYS) continue;
-    // exclusive prefix of c over the lanes, from the bits of c
+    // exclusive prefix of c (<= CK_KEYS here) over the lanes, from its bits
     int pos = 0;
 #pragma unroll
-    for (int b = 0; b < 6; ++b) pos += __popc(__ballot_sync(0xffffffffu, (c >> b) & 1) & lt) << b;
+    for (int b = 0; b < 5; ++b) pos += __popc(__ballot_sync(0xffffffffu, (c >> b) & 1) & lt) << b;
     if (ks) keys[pos++] = make_uint2(__float_as_uint(xs), (uint32_t)cs);
     while (mask) {
       const int k = __ffs(mask) - 1;
