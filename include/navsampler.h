@@ -17,6 +17,13 @@
  * per row of TokenSampler.SampleNext (Neuraval/Generation/TokenSampler.cs:10);
  * the LogitsProcessor entry points replace LogitsProcessor.* per row
  * (Neuraval/Generation/LogitsProcessor.cs:8-114). There is no CPU fallback.
+ *
+ * A sibling library of navcuda by design: the sampler keeps its own last
+ * status (ncb_sampler_last_status, not navcuda's ncb_cuda_last_status), so a
+ * C# caller checks it through its own ThrowIfError twin rather than through
+ * CudaDevice.ThrowIfError; the symbol names (ncb_sampler_*, ncb_sample_*,
+ * ncb_logits_*, ncb_vocab_shard_*, ncb_row_gather_*) do not collide with
+ * navcuda's, so the two can also be linked into one shared object.
  */
 #ifndef NAVSAMPLER_H
 #define NAVSAMPLER_H
@@ -55,6 +62,16 @@ extern "C" {
 #define NCB_FLAG_TIE_AT_DRAW 0x4u     /* drawn position in a group of equal values: the C#
                                          unstable sort (TokenSampler.cs:95) picks the id */
 #define NCB_FLAG_NONFINITE 0x8u       /* NaN/+inf value or no finite maximum: token -1 */
+/* API change from the reference, deliberate: for a row holding a NaN or +inf
+ * value (after the penalties and 1/T), or no finite value at all, the C#
+ * TokenSampler still returns an id, decided by how NaN compares inside its
+ * heap and sort and by the NaN weights that exp(inf - inf) produces
+ * (TokenSampler.cs:69-134); no test of the reference pins that id. This
+ * library returns -1 with NCB_FLAG_NONFINITE for the row instead and samples
+ * every other row normally, so the caller decides (the C# host class in the
+ * integration notes throws, which ends a generation loop that would have run
+ * on with an arbitrary id). Greedy rows are not affected: SampleGreedy's
+ * first strict maximum is well defined with NaN and inf and is reproduced. */
 #define NCB_FLAG_EXP_SLOW 0x10u       /* a weight needed the double-double exp path */
 #define NCB_FLAG_BAD_HISTORY 0x20u    /* frequency counting over a history longer than the handle's max: token -1 */
 #define NCB_FLAG_TIES_OVERFLOW 0x40u  /* ncb_sample_rows_noalloc_device and vocabulary-shard

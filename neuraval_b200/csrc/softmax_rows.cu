@@ -14,8 +14,18 @@
 // launched in groups whose data fits half of L2, so of the three reads of a
 // row only the first comes from HBM: one read and one write of the batch.
 //
+// Wide rows take softmax_rows_cluster_kernel instead: a cluster of SMX_CL
+// CTAs per row, CTA k owning the 32 chains 32k .. 32k+31. Chain t reads
+// columns t, t+256, ..., so CTA k reads one 128-byte piece of every 1 KiB of
+// the row (coalesced), keeps it in shared memory, and each chain stays whole
+// inside one CTA, added in element order by one thread. The CTAs exchange their
+// maxima through distributed shared memory, CTA 0 gathers the 256 chain sums
+// and runs the reference's tree, and every CTA writes e_j / p_0 for its own
+// columns: one read and one write of the batch from HBM, one expf per element.
+//
 // This translation unit is compiled with nvcc's default floating-point
 // contraction, as the reference is, so that expf is the same function.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <cfloat>
@@ -150,6 +160,98 @@ __global__ void __launch_bounds__(NT) softmax_rows_kernel(const float* in, float
   }
 }
 
+// Cluster of SMX_CL CTAs per row (see the header comment). pieces = ceil(cols /
+// 256); e[] holds this CTA's 32 columns of every piece: e[32 i + l] is column
+// 256 i + 32 k + l.
+constexpr int SMX_CL = 8;
+constexpr int SMX_CL_THREADS = 512;
+constexpr int SMX_CL_MAX_PIECES = 1536;  // 192 KiB of shared memory: cols <= 393216
+__global__ void __cluster_dims__(SMX_CL, 1, 1) __launch_bounds__(SMX_CL_THREADS)
+    softmax_rows_cluster_kernel(const float* in, float* out, int cols, int pieces) {
+  namespace cg = cooperative_groups;
+  extern __shared__ float e[];
+  __shared__ float s_red[SMX_CL_THREADS / 32];
+  __shared__ float s_max[SMX_CL];
+  __shared__ float s_sums[SMX_CHAINS];
+  __shared__ float s_rsum;
+  cg::cluster_group cl = cg::this_cluster();
+  const int k = (int)cl.block_rank();
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  constexpr int NW = SMX_CL_THREADS / 32;
+  const size_t row = blockIdx.x / SMX_CL;
+  const float* x = in + row * (size_t)cols;
+  float* y = out + row * (size_t)cols;
+  const int c0 = 32 * k + lane;  // this lane's column in piece 0
+  // ---- load this CTA's columns (warp w: pieces w, w + NW, ...) and its maximum,
+  // SMX_CL_INFLIGHT loads per lane in flight before any is stored --------------
+  constexpr int SMX_CL_INFLIGHT = 16;
+  float m = -FLT_MAX;
+  for (int i0 = warp; i0 < pieces; i0 += NW * SMX_CL_INFLIGHT) {
+    float v[SMX_CL_INFLIGHT];
+#pragma unroll
+    for (int u = 0; u < SMX_CL_INFLIGHT; ++u) {
+      const int i = i0 + u * NW, j = 256 * i + c0;
+      v[u] = (i < pieces && j < cols) ? __ldcs(x + j) : -FLT_MAX;
+    }
+#pragma unroll
+    for (int u = 0; u < SMX_CL_INFLIGHT; ++u) {
+      const int i = i0 + u * NW;
+      if (i < pieces) e[32 * i + lane] = v[u];
+      m = fmaxf(m, v[u]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) s_red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < NW ? s_red[lane] : -FLT_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+    if (lane < SMX_CL) *cl.map_shared_rank(&s_max[k], lane) = w;  // every CTA's slot k
+  }
+  cl.sync();
+  float rmax = -FLT_MAX;
+#pragma unroll
+  for (int r = 0; r < SMX_CL; ++r) rmax = fmaxf(rmax, s_max[r]);
+  // ---- e_j = expf(x_j - max), in place ---------------------------------------------
+  for (int i = warp; i < pieces; i += NW) {
+    const int j = 256 * i + c0;
+    if (j < cols) e[32 * i + lane] = expf(e[32 * i + lane] - rmax);
+  }
+  __syncthreads();
+  // ---- warp 0: chain 32 k + lane over its columns in order, to CTA 0 ---------------
+  if (warp == 0) {
+    float sum = 0.0f;
+    int i = 0;
+    for (; i + 8 <= pieces && 256 * (i + 7) + c0 < cols; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = e[32 * (i + u) + lane];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sum += v[u];
+    }
+    for (; i < pieces && 256 * i + c0 < cols; ++i) sum += e[32 * i + lane];
+    *cl.map_shared_rank(&s_sums[32 * k + lane], 0) = sum;
+  }
+  cl.sync();
+  // ---- CTA 0: the reference's tree over the 256 chain sums, total to every CTA -----
+  if (k == 0) {
+    for (int stride = SMX_CHAINS / 2; stride > 0; stride >>= 1) {
+      if (t < stride) s_sums[t] += s_sums[t + stride];
+      __syncthreads();
+    }
+    if (t < SMX_CL) *cl.map_shared_rank(&s_rsum, t) = s_sums[0];
+  }
+  cl.sync();
+  const float rsum = s_rsum;
+  // ---- outputs: e_j / sum for this CTA's columns ----------------------------------
+  for (int i = warp; i < pieces; i += NW) {
+    const int j = 256 * i + c0;
+    if (j < cols) __stcs(y + j, e[32 * i + lane] / rsum);
+  }
+}
+
 }  // namespace nvs
 
 extern "C" NCB_API int ncb_softmax_rows_device(const float* d_in, float* d_out, int rows, int cols,
@@ -158,8 +260,25 @@ extern "C" NCB_API int ncb_softmax_rows_device(const float* d_in, float* d_out, 
     return ncb_record_status(NCB_ERROR_INVALID_ARGUMENT);
   if ((reinterpret_cast<uintptr_t>(d_in) & 3u) != 0u || (reinterpret_cast<uintptr_t>(d_out) & 3u) != 0u)
     return ncb_record_status(NCB_ERROR_INVALID_ARGUMENT);
-  // rows go in launches whose data fits the L2 budget (passes 2 and 3 re-read it)
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // wide rows: one cluster per row, one HBM read and one write
+  const int pieces = (cols + nvs::SMX_CHAINS - 1) / nvs::SMX_CHAINS;
+  if (cols >= 8192 && pieces <= nvs::SMX_CL_MAX_PIECES &&
+      (long long)rows * nvs::SMX_CL <= 0x7FFFFFFFLL) {
+    const size_t smem = (size_t)pieces * 32 * sizeof(float);
+    static bool attr_set = false;  // the attribute is per function; setting it twice is harmless
+    if (!attr_set) {
+      if (cudaFuncSetAttribute(nvs::softmax_rows_cluster_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)(nvs::SMX_CL_MAX_PIECES * 32 * sizeof(float))) != cudaSuccess)
+        return ncb_record_status(NCB_ERROR_LAUNCH_FAILED);
+      attr_set = true;
+    }
+    nvs::softmax_rows_cluster_kernel<<<rows * nvs::SMX_CL, nvs::SMX_CL_THREADS, smem, st>>>(
+        d_in, d_out, cols, pieces);
+    return ncb_record_status(cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED);
+  }
+  // rows go in launches whose data fits the L2 budget (passes 2 and 3 re-read it)
   const size_t row_bytes = (size_t)cols * 4;
   int fit = (int)(nvs::SMX_L2_BYTES / row_bytes);
   if (fit < 1) fit = 1;

@@ -105,17 +105,23 @@ __device__ __forceinline__ uint32_t ck_group(const float4 (&x)[CK_LOADS], const 
   const float m = fmax3_nan(fmax3_nan(t[0], t[1], t[2]), fmax3_nan(t[3], t[4], t[5]),
                             fmax3_nan(fmax3_nan(t[6], t[7], t[8]), t[9], t[10]));
   if (__any_sync(0xffffffffu, !(m < INFINITY))) return CK_W_NONFINITE;
-  // the largest lane maxima, popped CK_RANK times (order-preserving keys;
-  // equal maxima count once per lane)
+  // the CK_RANK-th and CK_RANK/2-th largest lane maxima, counted with
+  // multiplicity (order-preserving keys): each round takes the largest
+  // remaining maximum and every lane holding it, until CK_RANK are counted
   uint32_t key = fkey(m);
   uint32_t k4 = 0u, k8 = 0u;
+  int taken = 0;
 #pragma unroll
   for (int r = 0; r < CK_RANK; ++r) {
-    const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
-    const unsigned hit = __ballot_sync(0xffffffffu, key == mx);
-    if (lane == __ffs(hit) - 1) key = 0u;
-    if (r == CK_RANK / 2 - 1) k4 = mx;
-    k8 = mx;
+    if (taken < CK_RANK) {
+      const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
+      const bool mine = key == mx;
+      const int now = taken + __popc(__ballot_sync(0xffffffffu, mine));
+      if (mine) key = 0u;
+      if (taken < CK_RANK / 2 && now >= CK_RANK / 2) k4 = mx;
+      if (now >= CK_RANK) k8 = mx;
+      taken = now;
+    }
   }
   for (int pass = 0; pass < 2; ++pass) {
     const float t0 = kval(pass == 0 ? k8 : k4);
@@ -237,21 +243,35 @@ __global__ void __launch_bounds__(CR_THREADS, 1) topk_chunk_kernel(const __grid_
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // the finish kernel may be scheduled now; it waits for this grid to complete
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  auto chunk = [&](int t, const float*& lrow, int& j, int& q0, int& q1, CkRow& g) {
-    const int row = t / J;
-    j = t - row * J;
+  // chunk (row, j): part j of the row's float4 body, [q0, q1). Callers walk
+  // the chunks with a fixed stride and carry (row, j) along (no division by J
+  // per chunk); j * n4 stays below 2^32 (J <= CK_MAX_CHUNKS, n4 < 2^26).
+  auto chunk = [&](int row, int j, const float*& lrow, int& q0, int& q1, CkRow& g) {
     lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * a.V;
     g = ck_row(lrow, lo, hi);
-    q0 = (int)((long long)j * g.n4 / J);
-    q1 = (int)((long long)(j + 1) * g.n4 / J);
-    return row;
+    q0 = (int)(((uint32_t)j * (uint32_t)g.n4) / (uint32_t)J);
+    q1 = (int)(((uint32_t)(j + 1) * (uint32_t)g.n4) / (uint32_t)J);
+  };
+  // (row, j) of chunk t0c + first, advanced by `stride` chunks
+  auto first_chunk = [&](int first, int& row, int& j) {
+    row = (t0c + first) / J;
+    j = t0c + first - row * J;
+  };
+  auto advance = [&](int stride, int& row, int& j) {
+    j += stride;
+    while (j >= J) {
+      j -= J;
+      ++row;
+    }
   };
   if (warp == CR_CONSUMERS) {
     // producer: one elected lane issues the copies
     if (lane == 0) {
       uint64_t policy;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-      for (int i = 0; i < n; ++i) {
+      int row, j;
+      first_chunk(0, row, j);
+      for (int i = 0; i < n; ++i, advance(1, row, j)) {
         const int st = i % CR_STAGES;
         if (i >= CR_STAGES && !cr_wait(&empty[st], (uint32_t)(((i / CR_STAGES) - 1) & 1))) {
           atomicOr(&s_abort, 1);
@@ -259,9 +279,9 @@ __global__ void __launch_bounds__(CR_THREADS, 1) topk_chunk_kernel(const __grid_
         }
         if (*(volatile int*)&s_abort) break;
         const float* lrow;
-        int j, q0, q1;
+        int q0, q1;
         CkRow g;
-        chunk(t0c + i, lrow, j, q0, q1, g);
+        chunk(row, j, lrow, q0, q1, g);
         const uint32_t bytes = (uint32_t)(q1 - q0) * 16u;
         mbar_arrive_expect_tx(&full[st], bytes);
         if (bytes)
@@ -271,12 +291,14 @@ __global__ void __launch_bounds__(CR_THREADS, 1) topk_chunk_kernel(const __grid_
     }
   } else {
     const int team = warp / CK_WARPS, sub = warp % CK_WARPS;
-    for (int i = team; i < n; i += CR_TEAMS) {
+    int row, j;
+    first_chunk(team, row, j);
+    for (int i = team; i < n; i += CR_TEAMS, advance(CR_TEAMS, row, j)) {
       const int st = i % CR_STAGES;
       const float* lrow;
-      int j, q0, q1;
+      int q0, q1;
       CkRow g;
-      const int row = chunk(t0c + i, lrow, j, q0, q1, g);
+      chunk(row, j, lrow, q0, q1, g);
       const size_t gidx = ((size_t)row * J + j) * CK_WARPS + sub;
       const bool ok = cr_wait(&full[st], (uint32_t)((i / CR_STAGES) & 1));
       if (!ok) {

@@ -3,6 +3,7 @@
 // Neuraval/Generation/*.cs) over libnavsampler's C ABI (navsampler.h). Same
 // names, argument meaning and argument checks, in the same order, with the
 // exception types of the C# code:
+//   ArgumentException           -> neuraval::ArgumentException
 //   ArgumentNullException       -> neuraval::ArgumentNullException
 //   ArgumentOutOfRangeException -> neuraval::ArgumentOutOfRangeException
 //   CudaException               -> neuraval::CudaException (a non-OK status)
@@ -12,18 +13,27 @@
 // scratch), and TokenSampler / LogitsProcessor borrow it.
 #pragma once
 
+#include <algorithm>
 #include <climits>
 #include <cstdint>
+#include <cstring>
+#include <functional>
+#include <memory>
 #include <optional>
 #include <random>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
+#include <cuda_runtime.h>
+
 #include "navsampler.h"
 
 namespace neuraval {
 
+struct ArgumentException : std::invalid_argument {
+  explicit ArgumentException(const std::string& param) : std::invalid_argument(param) {}
+};
 struct ArgumentNullException : std::invalid_argument {
   explicit ArgumentNullException(const std::string& param) : std::invalid_argument(param) {}
 };
@@ -271,6 +281,141 @@ class LogitsProcessor {
 
  private:
   Device& d_;
+};
+
+// GenerationFinishReason (GenerationFinishReason.cs) and GenerationResult
+// (GenerationResult.cs:7-27).
+enum class GenerationFinishReason { MaxNewTokens, StopToken };
+struct GenerationResult {
+  std::vector<int> GeneratedTokenIds;
+  GenerationFinishReason FinishReason = GenerationFinishReason::MaxNewTokens;
+};
+
+// TextGenerator.Generate (TextGenerator.cs:19-51): the decode loop around
+// TokenSampler.SampleNext. The model is a callable from the context window's
+// token ids to the last position's logits (_model.Forward followed by
+// ExtractLastPositionLogits, :34-35); the context is the sequence trimmed to
+// the model's last maxPositionEmbeddings ids (TrimToContextWindow,
+// :128-139). The history passed to the sampler is the generated ids only
+// (:37), and the random source is drawn once per non-greedy step and never
+// on a greedy step (TokenSampler.cs:125). Without a random source the loop
+// seeds its own from options.Seed(), as :26 does (a std::mt19937_64, not
+// .NET's Random: the draws differ from the reference's for the same seed).
+class TextGenerator {
+ public:
+  using Model = std::function<std::vector<float>(const std::vector<int>& context)>;
+  // The device-resident handoff: the model leaves the last position's logits
+  // in device memory it owns (`vocab` floats, complete in stream order on
+  // `stream`) and returns their address; the sampler reads them in place
+  // (the D2H copy of ModernDecoderModel.cs:169-170 is gone).
+  using DeviceModel = std::function<const float*(const std::vector<int>& context,
+                                                 cudaStream_t stream)>;
+
+  TextGenerator(Device& device, int maxPositionEmbeddings)
+      : device_(device), sampler_(device), max_positions_(maxPositionEmbeddings) {
+    if (maxPositionEmbeddings < 1) throw ArgumentOutOfRangeException("maxPositionEmbeddings");
+  }
+
+  GenerationResult Generate(const Model& model, const std::vector<int>& promptTokenIds,
+                            const GenerationOptions& options, Random* random = nullptr) const {
+    if (!model) throw ArgumentNullException("model");
+    if (promptTokenIds.empty()) throw ArgumentException("promptTokenIds");
+    std::optional<DefaultRandom> own;
+    if (!random) random = &own.emplace(SeedOf(options));
+    std::vector<int> sequence(promptTokenIds), generated;
+    GenerationResult result;
+    for (int step = 0; step < options.MaxNewTokens(); ++step) {
+      const std::vector<float> logits = model(Trim(sequence));
+      const int next = sampler_.SampleNext(logits, options, generated, *random);
+      generated.push_back(next);
+      sequence.push_back(next);
+      if (IsStop(options, next)) {
+        result.FinishReason = GenerationFinishReason::StopToken;
+        break;
+      }
+    }
+    result.GeneratedTokenIds = std::move(generated);
+    return result;
+  }
+
+  // Generate with the logits left on the device. Per step: the model's
+  // launches, one 12-byte copy to the device (the history length and the
+  // uniform, from pinned memory), ncb_sample_rows_device writing the token
+  // straight into the device history (its next slot), and one 4-byte copy
+  // back for the stop test and the next context.
+  GenerationResult GenerateDevice(const DeviceModel& model, int vocab,
+                                  const std::vector<int>& promptTokenIds,
+                                  const GenerationOptions& options, cudaStream_t stream,
+                                  Random* random = nullptr) const {
+    if (!model) throw ArgumentNullException("model");
+    if (promptTokenIds.empty()) throw ArgumentException("promptTokenIds");
+    if (vocab <= 0) throw ArgumentOutOfRangeException("vocab");
+    std::optional<DefaultRandom> own;
+    if (!random) random = &own.emplace(SeedOf(options));
+    const int cap = std::max(1, options.MaxNewTokens());
+    auto dev_free = [](void* p) { cudaFree(p); };
+    auto host_free = [](void* p) { cudaFreeHost(p); };
+    void* p = nullptr;
+    cuda(cudaMalloc(&p, sizeof(int32_t) * (size_t)(cap + 4)), "cudaMalloc");
+    std::unique_ptr<void, decltype(dev_free)> dmem(p, dev_free);
+    p = nullptr;
+    cuda(cudaMallocHost(&p, sizeof(int32_t) * 4), "cudaMallocHost");
+    std::unique_ptr<void, decltype(host_free)> hmem(p, host_free);
+    int32_t* d_hist = static_cast<int32_t*>(dmem.get());  // [cap] generated ids
+    int32_t* d_step = d_hist + cap;                       // {0, n, bits of u}
+    int32_t* h_step = static_cast<int32_t*>(hmem.get());  // pinned {0, n, u, token}
+    const NcbSamplerParams prm = options.ToParams();
+    std::vector<int> sequence(promptTokenIds), generated;
+    GenerationResult result;
+    for (int step = 0; step < options.MaxNewTokens(); ++step) {
+      const float* d_logits = model(Trim(sequence), stream);
+      if (!d_logits) throw ArgumentNullException("logits");
+      const float u = options.Greedy() ? 0.0f : static_cast<float>(random->NextDouble());
+      h_step[0] = 0;
+      h_step[1] = step;
+      std::memcpy(&h_step[2], &u, sizeof(float));
+      cuda(cudaMemcpyAsync(d_step, h_step, 3 * sizeof(int32_t), cudaMemcpyHostToDevice, stream),
+           "cudaMemcpyAsync");
+      check(ncb_sample_rows_device(device_.handle(), d_logits, 1, vocab, d_hist, d_step,
+                                   reinterpret_cast<const float*>(d_step + 2), &prm,
+                                   d_hist + step, nullptr, nullptr, stream),
+            "ncb_sample_rows_device");
+      cuda(cudaMemcpyAsync(&h_step[3], d_hist + step, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                           stream),
+           "cudaMemcpyAsync");
+      cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+      const int next = h_step[3];
+      if (next < 0) throw CudaException(NCB_ERROR_INVALID_ARGUMENT, "GenerateDevice: row not sampled");
+      generated.push_back(next);
+      sequence.push_back(next);
+      if (IsStop(options, next)) {
+        result.FinishReason = GenerationFinishReason::StopToken;
+        break;
+      }
+    }
+    result.GeneratedTokenIds = std::move(generated);
+    return result;
+  }
+
+ private:
+  static uint64_t SeedOf(const GenerationOptions& o) {
+    return o.Seed() ? static_cast<uint64_t>(*o.Seed()) : std::random_device{}();
+  }
+  static bool IsStop(const GenerationOptions& o, int token) {
+    const std::vector<int>& s = o.StopTokenIds();
+    return std::find(s.begin(), s.end(), token) != s.end();
+  }
+  static void cuda(cudaError_t e, const char* where) {
+    if (e != cudaSuccess) throw CudaException(NCB_ERROR_LAUNCH_FAILED, where);
+  }
+  std::vector<int> Trim(const std::vector<int>& sequence) const {
+    if ((int)sequence.size() <= max_positions_) return sequence;
+    return std::vector<int>(sequence.end() - max_positions_, sequence.end());
+  }
+
+  Device& device_;
+  TokenSampler sampler_;
+  int max_positions_;
 };
 
 }  // namespace neuraval

@@ -176,6 +176,117 @@ static void processor_tests(Device& dev) {
          "ApplyRepetitionPenalty null history");
 }
 
+// TextGenerator.Generate (TextGenerator.cs:19-51) over a toy model: the logits
+// are a fixed function of the context window, so every step can be replayed.
+static std::vector<float> toy_logits(const std::vector<int>& ctx, int V) {
+  uint64_t h = 1469598103934665603ull;
+  for (int t : ctx) h = (h ^ (uint64_t)(uint32_t)t) * 1099511628211ull;
+  std::vector<float> x(V);
+  for (int i = 0; i < V; ++i) {
+    uint64_t z = h + 0x9E3779B97F4A7C15ull * (uint64_t)(i + 1);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    x[i] = (float)((double)(z >> 11) * 0x1p-53 * 12.0 - 6.0);  // uniform in [-6, 6)
+  }
+  return x;
+}
+
+// Counts the draws and remembers them.
+struct Counting final : Random {
+  DefaultRandom r;
+  std::vector<double> seen;
+  explicit Counting(uint64_t seed) : r(seed) {}
+  double NextDouble() override {
+    seen.push_back(r.NextDouble());
+    return seen.back();
+  }
+};
+
+static void generator_tests(Device& dev) {
+  const int V = 4096, window = 16;
+  int forwards = 0;
+  size_t longest = 0;
+  TextGenerator gen(dev, window);
+  const TextGenerator::Model model = [&](const std::vector<int>& ctx) {
+    ++forwards;
+    longest = std::max(longest, ctx.size());
+    return toy_logits(ctx, V);
+  };
+  const std::vector<int> prompt = {5, 17, 42};
+  const std::vector<int> none;
+  EXPECT(throws<ArgumentException>([&] { gen.Generate(model, {}, GenerationOptions::Default(none)); }),
+         "Generate empty prompt");
+
+  // greedy steps never draw (TokenSampler.cs:25-26 takes the greedy path first)
+  const auto greedy = GenerationOptions::Create(true, 1.0f, 1.0f, INT_MAX, 1.1f, 24, none);
+  Counting rg(7);
+  GenerationResult res = gen.Generate(model, prompt, greedy, &rg);
+  EXPECT(rg.seen.empty(), "greedy steps draw nothing");
+  EXPECT(res.GeneratedTokenIds.size() == 24 && res.FinishReason == GenerationFinishReason::MaxNewTokens,
+         "greedy runs to MaxNewTokens");
+  EXPECT(longest <= (size_t)window, "context trimmed to the window");
+
+  // filtered steps draw exactly once each, in step order; replaying the steps
+  // through SampleNext with the same draws gives the same tokens
+  const auto filt = GenerationOptions::Create(false, 0.8f, 0.9f, 40, 1.1f, 24, none);
+  Counting rf(11);
+  forwards = 0;
+  res = gen.Generate(model, prompt, filt, &rf);
+  EXPECT(rf.seen.size() == 24 && forwards == 24, "one draw and one forward per filtered step");
+  {
+    TokenSampler ts(dev);
+    std::vector<int> seq(prompt), hist;
+    bool same = true;
+    for (size_t i = 0; i < res.GeneratedTokenIds.size(); ++i) {
+      std::vector<int> ctx(seq.size() > (size_t)window ? seq.end() - window : seq.begin(), seq.end());
+      Scripted one({rf.seen[i]});
+      const int t = ts.SampleNext(toy_logits(ctx, V), filt, hist, one);
+      same = same && t == res.GeneratedTokenIds[i];
+      hist.push_back(t);
+      seq.push_back(t);
+    }
+    EXPECT(same, "each step is SampleNext on the window's logits, the generated ids and its draw");
+  }
+
+  // a stop id ends the loop at its first occurrence, the stop id included (:40-47)
+  const int stop = res.GeneratedTokenIds[9];
+  size_t first = 0;
+  while (res.GeneratedTokenIds[first] != stop) ++first;
+  const auto filt_stop = GenerationOptions::Create(false, 0.8f, 0.9f, 40, 1.1f, 24, {stop});
+  Counting rs(11);
+  GenerationResult rstop = gen.Generate(model, prompt, filt_stop, &rs);
+  EXPECT(rstop.FinishReason == GenerationFinishReason::StopToken &&
+             rstop.GeneratedTokenIds.size() == first + 1 && rstop.GeneratedTokenIds.back() == stop &&
+             rs.seen.size() == first + 1,
+         "stop token ends generation");
+
+  // device-resident logits: the same tokens and draws as the host loop
+  float* d_logits = nullptr;
+  if (cudaMalloc(reinterpret_cast<void**>(&d_logits), sizeof(float) * V) != cudaSuccess) {
+    EXPECT(false, "cudaMalloc for the device model");
+    return;
+  }
+  const TextGenerator::DeviceModel dmodel = [&](const std::vector<int>& ctx, cudaStream_t st) {
+    const std::vector<float> x = toy_logits(ctx, V);
+    cudaMemcpyAsync(d_logits, x.data(), sizeof(float) * V, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);  // x is a temporary
+    return static_cast<const float*>(d_logits);
+  };
+  cudaStream_t st = nullptr;
+  cudaStreamCreate(&st);
+  for (const GenerationOptions* o : {&greedy, &filt, &filt_stop}) {
+    Counting a(23), b(23);
+    const GenerationResult h = gen.Generate(model, prompt, *o, &a);
+    const GenerationResult d = gen.GenerateDevice(dmodel, V, prompt, *o, st, &b);
+    EXPECT(h.GeneratedTokenIds == d.GeneratedTokenIds && h.FinishReason == d.FinishReason &&
+               a.seen == b.seen,
+           "device-resident loop equals the host loop");
+  }
+  cudaStreamDestroy(st);
+  cudaFree(d_logits);
+}
+
 int main(int argc, char** argv) {
   const bool options_only = argc > 1 && std::strcmp(argv[1], "--options-only") == 0;
   options_tests();
@@ -183,6 +294,7 @@ int main(int argc, char** argv) {
     Device dev(0, 4, 4096, 64);
     sampler_tests(dev);
     processor_tests(dev);
+    generator_tests(dev);
   }
   std::printf("%d checks, %d failed\n", g_run, g_fail);
   return g_fail == 0 ? 0 : 1;

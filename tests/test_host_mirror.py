@@ -1,6 +1,7 @@
 """The C++ host mirror (neuraval_b200/host/neuraval_generation.hpp) compiled with
 g++ against libnavsampler and run on the reference's own test cases
-(tests/cpp/host_mirror_tests.cpp)."""
+(tests/cpp/host_mirror_tests.cpp), including a TextGenerator decode loop over a
+toy model (host logits and device-resident logits)."""
 import os
 import subprocess
 import sys
@@ -8,6 +9,7 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 
 def _build(tmp_path):
@@ -22,8 +24,11 @@ def _build(tmp_path):
     subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Wextra",
                     "-I", os.path.join(ROOT, "include"),
                     "-I", os.path.join(ROOT, "neuraval_b200", "host"), "-I", str(tmp_path),
+                    "-I", os.path.join(CUDA, "include"),
                     os.path.join(ROOT, "tests", "cpp", "host_mirror_tests.cpp"),
-                    "-L", libdir, "-lnavsampler", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                    "-L", libdir, "-lnavsampler", f"-Wl,-rpath,{libdir}",
+                    "-L", os.path.join(CUDA, "lib64"), "-lcudart", f"-Wl,-rpath,{os.path.join(CUDA, 'lib64')}",
+                    "-o", str(exe)],
                    check=True)
     return exe
 

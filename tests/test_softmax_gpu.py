@@ -58,6 +58,21 @@ def _cases():
     x[4, 3] = -0.0
     x[5, ::2] = 88.0           # large equal maxima
     yield "special", x
+    # rows of 8192+ columns take the cluster kernel (one cluster of CTAs per row)
+    yield "3x8195", (rng.standard_normal((3, 8195)) * 4).astype(np.float32)
+    yield "2x40003", (rng.standard_normal((2, 40003)) * 6).astype(np.float32)
+    w = (rng.standard_normal((8, 9000)) * 5).astype(np.float32)
+    w[0, :300] = -np.inf
+    w[1, :] = -np.inf
+    w[2, 4097] = np.nan
+    w[3, 8999] = np.inf
+    w[4, :] = 0.0
+    w[4, 257] = -0.0
+    w[5, 1::3] = 88.0
+    w[6, 8191] = 1e30         # one huge maximum in the last piece
+    yield "special_wide", w
+    yield "1x393216", (rng.standard_normal((1, 393216)) * 3).astype(np.float32)
+    yield "1x393217", (rng.standard_normal((1, 393217)) * 3).astype(np.float32)
 
 
 @pytest.mark.parametrize("name,x", list(_cases()), ids=[c[0] for c in _cases()])
@@ -84,6 +99,8 @@ def test_softmax_full_logits_batch():
 def test_softmax_in_place_and_errors():
     rng = np.random.default_rng(3)
     x = rng.standard_normal((9, 3001), dtype=np.float32)
+    assert np.array_equal(_ours(x, inplace=True), _ours(x))
+    x = rng.standard_normal((5, 20001), dtype=np.float32)  # the cluster kernel
     assert np.array_equal(_ours(x, inplace=True), _ours(x))
     lib = native.load()
     assert lib.ncb_softmax_rows_device(None, None, 0, 4, None) == native.NCB_ERROR_INVALID_ARGUMENT
