@@ -1308,7 +1308,7 @@ NCB_API int ncb_row_gather_setup(NcbSampler* h, int ranks, int me, int rows_tota
   std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  const nvs::RgLayout l = nvs::rg_layout(rows_total, h->max_rows);
+  const nvs::RgLayout l = nvs::rg_layout(rows_total);
   void* area = nullptr;
   if (cudaMalloc(&area, l.bytes) != cudaSuccess) return set_status(NCB_ERROR_ALLOC_FAILED);
   cudaIpcMemHandle_t hd;
@@ -1384,7 +1384,7 @@ NCB_API int ncb_sample_rows_gather_device(NcbSampler* h, const float* d_logits, 
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   int32_t* st_tok = reinterpret_cast<int32_t*>(h->rg_area + h->rg_layout.staging_off);
-  uint32_t* st_flg = reinterpret_cast<uint32_t*>(st_tok + h->max_rows);
+  uint32_t* st_flg = reinterpret_cast<uint32_t*>(st_tok + h->rg_rows_total);
   if (rows > 0) {
     st = launch_sample(h, d_logits, rows, vocab, d_hist, d_hist_offsets, d_uniforms, params, st_tok,
                        st_flg, nullptr, stream);
@@ -1396,7 +1396,6 @@ NCB_API int ncb_sample_rows_gather_device(NcbSampler* h, const float* d_logits, 
   ga.ranks = h->rg_ranks;
   ga.me = h->rg_me;
   ga.rows_total = h->rg_rows_total;
-  ga.max_rows = h->max_rows;
   ga.row_begin = row_begin;
   ga.rows = rows;
   ga.out_tok = d_tokens_all;

@@ -7,7 +7,9 @@
 // area (one cudaMalloc, shared with the others by CUDA IPC):
 //   copy[2][rows_total]     (token, flags) pairs of all rows, 8 bytes a row; a
 //                           call of epoch e uses copy e & 1
-//   staging[2][max_rows]    this GPU's own rows, written by the sampling kernels
+//   staging[2][rows_total]  this GPU's own rows, written by the sampling kernels
+//                           (sized by rows_total, which every GPU shares, so the
+//                           flags sit at the same offset in every GPU's area)
 //   flags[16]               flags[g] = e: GPU g's rows of call e are here
 //   epoch                   the last call's epoch (this GPU's own counter)
 // row_gather_kernel, after the sampling kernels of call e: stores the staged
@@ -33,11 +35,11 @@ struct RgLayout {
   size_t epoch_off;
   size_t bytes;
 };
-inline RgLayout rg_layout(int rows_total, int max_rows) {
+inline RgLayout rg_layout(int rows_total) {
   RgLayout l;
   const size_t copies = (size_t)2 * rows_total * 8;
   l.staging_off = (copies + 255) / 256 * 256;
-  l.flags_off = l.staging_off + ((size_t)2 * max_rows * 4 + 255) / 256 * 256;
+  l.flags_off = l.staging_off + ((size_t)2 * rows_total * 4 + 255) / 256 * 256;
   l.epoch_off = l.flags_off + 128;
   l.bytes = l.flags_off + 256;
   return l;
@@ -46,7 +48,7 @@ inline RgLayout rg_layout(int rows_total, int max_rows) {
 struct RgArgs {
   char* area[PX_MAX];   // every GPU's area as mapped here (own included)
   RgLayout l;
-  int ranks, me, rows_total, max_rows, row_begin, rows;
+  int ranks, me, rows_total, row_begin, rows;
   int32_t* out_tok;     // [rows_total]
   uint32_t* out_flg;    // [rows_total], may be null
 };
@@ -64,7 +66,7 @@ __global__ void __launch_bounds__(RG_THREADS) row_gather_kernel(const __grid_con
   const uint32_t e = s_epoch;
   const int c = (int)(e & 1u);
   const int32_t* st_tok = reinterpret_cast<const int32_t*>(own + g.l.staging_off);
-  const uint32_t* st_flg = reinterpret_cast<const uint32_t*>(st_tok + g.max_rows);
+  const uint32_t* st_flg = reinterpret_cast<const uint32_t*>(st_tok + g.rows_total);
   for (int i = tid; i < g.rows; i += RG_THREADS) {
     const uint2 v = make_uint2((uint32_t)st_tok[i], st_flg[i]);
     for (int p = 0; p < g.ranks; ++p)
