@@ -250,9 +250,11 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* sampler, float* d_probs, 
 /* The same exchange done by the library through peer memory, without a
  * collective (no reference counterpart). Each GPU's handle owns one exchange
  * area: ncb_vocab_shard_peer_setup allocates it and writes its CUDA IPC handle
- * (ncb_peer_handle_bytes() bytes); the caller gives every handle all handles
- * in shard order (ncb_vocab_shard_peer_connect; handles exported by the same
- * process resolve without IPC). Per call, on every GPU in the same order:
+ * with what the area is laid out for (ncb_peer_handle_bytes() bytes); the
+ * caller gives every handle all handles in shard order
+ * (ncb_vocab_shard_peer_connect; handles exported by the same process resolve
+ * without IPC). Connect returns NCB_ERROR_INVALID_ARGUMENT unless every handle
+ * was set up for the same shard count and the same max_rows. Per call, on every GPU in the same order:
  * ncb_vocab_shard_push_peer_device (shard kernel, then its records are stored
  * into every GPU's area over NVLink and an epoch flag is released there) and
  * ncb_vocab_shard_merge_peer_device (waits for every shard's flag, merges,
@@ -281,7 +283,9 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* sampler, int rows, int
  * gathered through peer memory instead of a collective. Each GPU's handle owns
  * one gather area: ncb_row_gather_setup allocates it for rows_total rows and
  * writes its CUDA IPC handle (ncb_peer_handle_bytes() bytes); the caller gives
- * every handle all handles in rank order (ncb_row_gather_connect). Per call,
+ * every handle all handles in rank order (ncb_row_gather_connect, which returns
+ * NCB_ERROR_INVALID_ARGUMENT unless every handle was set up for the same ranks
+ * and rows_total). Per call,
  * on every GPU in the same order: ncb_sample_rows_gather_device samples this
  * GPU's rows [row_begin, row_begin + rows) (arguments as ncb_sample_rows_device,
  * rows <= max_rows), stores their tokens and flags into every GPU's area over

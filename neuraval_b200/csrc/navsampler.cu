@@ -1080,7 +1080,42 @@ NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, i
 
 extern "C" {
 
-NCB_API int ncb_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+}  // extern "C"
+
+// What each GPU publishes for a peer-memory exchange: its area's CUDA IPC
+// handle and what the area was laid out for. Every GPU's area must have the
+// same layout (a peer writes at offsets computed from its own), so connect
+// refuses blobs that disagree instead of corrupting a peer's memory.
+struct PeerBlob {
+  cudaIpcMemHandle_t ipc;
+  uint32_t magic;  // kPeerMagic
+  uint32_t kind;   // kPeerVocab or kPeerRows
+  uint32_t size;   // vocabulary shards: rows per call; row gather: rows of the whole batch
+  uint32_t ranks;
+};
+constexpr uint32_t kPeerMagic = 0x5850564Eu;  // "NVPX"
+constexpr uint32_t kPeerVocab = 1u, kPeerRows = 2u;
+
+static void write_blob(void* out, const cudaIpcMemHandle_t& hd, uint32_t kind, int size, int ranks) {
+  PeerBlob b{};
+  b.ipc = hd;
+  b.magic = kPeerMagic;
+  b.kind = kind;
+  b.size = (uint32_t)size;
+  b.ranks = (uint32_t)ranks;
+  std::memcpy(out, &b, sizeof(b));
+}
+
+// Blob s of `handles` if it agrees with (kind, size, ranks), else false.
+static bool read_blob(const void* handles, int s, uint32_t kind, int size, int ranks, PeerBlob* b) {
+  std::memcpy(b, static_cast<const char*>(handles) + (size_t)s * sizeof(PeerBlob), sizeof(*b));
+  return b->magic == kPeerMagic && b->kind == kind && b->size == (uint32_t)size &&
+         b->ranks == (uint32_t)ranks;
+}
+
+extern "C" {
+
+NCB_API int ncb_peer_handle_bytes(void) { return (int)sizeof(PeerBlob); }
 
 NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* h, int shards, int me, void* handle_out) {
   if (!h) return set_status(NCB_ERROR_NOT_INITIALIZED);
@@ -1098,7 +1133,7 @@ NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* h, int shards, int me, void* 
     cudaFree(area);
     return set_status(NCB_ERROR_INIT_FAILED);
   }
-  std::memcpy(handle_out, &hd, sizeof(hd));
+  write_blob(handle_out, hd, kPeerVocab, h->max_rows, shards);
   {
     std::lock_guard<std::mutex> lk2(g_px_mu);
     std::array<char, sizeof(cudaIpcMemHandle_t)> key;
@@ -1119,11 +1154,17 @@ NCB_API int ncb_vocab_shard_peer_connect(NcbSampler* h, const void* handles) {
   std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  const char* hb = static_cast<const char*>(handles);
+  for (int s = 0; s < h->px_shards; ++s) {
+    PeerBlob b;
+    if (!read_blob(handles, s, kPeerVocab, h->max_rows, h->px_shards, &b))
+      return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  }
   for (int s = 0; s < h->px_shards; ++s) {
     if (s == h->px_me) continue;
+    PeerBlob b;
+    read_blob(handles, s, kPeerVocab, h->max_rows, h->px_shards, &b);
     std::array<char, sizeof(cudaIpcMemHandle_t)> key;
-    std::memcpy(key.data(), hb + (size_t)s * sizeof(cudaIpcMemHandle_t), key.size());
+    std::memcpy(key.data(), &b.ipc, key.size());
     char* local = nullptr;
     {
       std::lock_guard<std::mutex> lk2(g_px_mu);
@@ -1317,7 +1358,7 @@ NCB_API int ncb_row_gather_setup(NcbSampler* h, int ranks, int me, int rows_tota
     cudaFree(area);
     return set_status(NCB_ERROR_INIT_FAILED);
   }
-  std::memcpy(handle_out, &hd, sizeof(hd));
+  write_blob(handle_out, hd, kPeerRows, rows_total, ranks);
   {
     std::lock_guard<std::mutex> lk2(g_px_mu);
     std::array<char, sizeof(cudaIpcMemHandle_t)> key;
@@ -1339,11 +1380,17 @@ NCB_API int ncb_row_gather_connect(NcbSampler* h, const void* handles) {
   std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  const char* hb = static_cast<const char*>(handles);
+  for (int s = 0; s < h->rg_ranks; ++s) {
+    PeerBlob b;
+    if (!read_blob(handles, s, kPeerRows, h->rg_rows_total, h->rg_ranks, &b))
+      return set_status(NCB_ERROR_INVALID_ARGUMENT);
+  }
   for (int s = 0; s < h->rg_ranks; ++s) {
     if (s == h->rg_me) continue;
+    PeerBlob b;
+    read_blob(handles, s, kPeerRows, h->rg_rows_total, h->rg_ranks, &b);
     std::array<char, sizeof(cudaIpcMemHandle_t)> key;
-    std::memcpy(key.data(), hb + (size_t)s * sizeof(cudaIpcMemHandle_t), key.size());
+    std::memcpy(key.data(), &b.ipc, key.size());
     char* local = nullptr;
     {
       std::lock_guard<std::mutex> lk2(g_px_mu);

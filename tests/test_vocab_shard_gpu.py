@@ -248,3 +248,31 @@ def test_peer_exchange_two_gpus():
         so.bind(("127.0.0.1", 0))
         port = so.getsockname()[1]
     mp.start_processes(_peer_rank_main, args=(2, port), nprocs=2, start_method="spawn", join=True)
+
+
+def test_peer_connect_rejects_mismatched_layouts(navlib):
+    """A GPU writes into a peer's area at offsets computed from its own layout,
+    so connect refuses handles set up for another shard count, row count or
+    exchange (no kernel runs here)."""
+    from neuraval_b200.sampler import CudaTokenSampler
+    mk = lambda rows: CudaTokenSampler(0, max_rows=rows, max_vocab=4096, max_history=64)
+    ss = [mk(16), mk(32), mk(16), mk(16), mk(8), mk(8), mk(8), mk(8)]
+    try:
+        a, b, c = ss[0].peer_setup(2, 0), ss[1].peer_setup(2, 1), ss[2].peer_setup(2, 1)
+        with pytest.raises(native.NcbError):
+            ss[0].peer_connect(a + b)          # max_rows 16 against 32
+        ss[0].peer_connect(a + c)              # the same layout connects
+        d = ss[3].peer_setup(3, 0)
+        with pytest.raises(native.NcbError):
+            ss[3].peer_connect(d + c + c)      # set up for 3 shards, peers for 2
+        r0, r1 = ss[4].row_gather_setup(2, 0, 100), ss[5].row_gather_setup(2, 1, 101)
+        with pytest.raises(native.NcbError):
+            ss[4].row_gather_connect(r0 + r1)  # rows_total 100 against 101
+        with pytest.raises(native.NcbError):
+            ss[4].row_gather_connect(r0 + c)   # a vocabulary-shard handle
+        r2 = ss[6].row_gather_setup(2, 1, 100)
+        ss[4].row_gather_connect(r0 + r2)
+        assert len(r0) == native.load().ncb_peer_handle_bytes()
+    finally:
+        for s in ss:
+            s.close()
