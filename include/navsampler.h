@@ -288,11 +288,13 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* sampler, int rows, int
  * and rows_total). Per call,
  * on every GPU in the same order: ncb_sample_rows_gather_device samples this
  * GPU's rows [row_begin, row_begin + rows) (arguments as ncb_sample_rows_device,
- * rows <= max_rows), stores their tokens and flags into every GPU's area over
- * NVLink, releases this call's flag there, waits (bounded, about 2 s) for every
- * GPU's flag and writes all rows_total tokens (and flags, may be NULL) to
- * d_tokens_all / d_flags_all. A wait that gives up returns every token as -1
- * with NCB_FLAG_PEER_TIMEOUT. Asynchronous on `stream`. */
+ * rows <= max_rows; the GPUs' ranges together cover [0, rows_total) once),
+ * stores their tokens and flags, tagged with the call's epoch, into every GPU's
+ * area over NVLink, waits (bounded, about 2 s) until every row of its own area
+ * carries the epoch and writes all rows_total tokens (and flags, may be NULL)
+ * to d_tokens_all / d_flags_all. A row still missing when the wait gives up
+ * (a peer that stopped, or a range no GPU covered) comes back as -1 with
+ * NCB_FLAG_PEER_TIMEOUT. Asynchronous on `stream`. */
 NCB_API int ncb_row_gather_setup(NcbSampler* sampler, int ranks, int me, int rows_total,
                                  void* handle_out);
 NCB_API int ncb_row_gather_connect(NcbSampler* sampler, const void* handles);

@@ -5,22 +5,22 @@
 // own, so a batch split by rows over G GPUs needs no exchange to sample; each
 // GPU only needs every other GPU's tokens afterwards. Each GPU owns one gather
 // area (one cudaMalloc, shared with the others by CUDA IPC):
-//   copy[2][rows_total]     (token, flags) pairs of all rows, 8 bytes a row; a
-//                           call of epoch e uses copy e & 1
+//   copy[2][rows_total][2]  64-bit words: (token, epoch) and (flags, epoch) of
+//                           every row; a call of epoch e uses copy e & 1
 //   staging[2][rows_total]  this GPU's own rows, written by the sampling kernels
-//                           (sized by rows_total, which every GPU shares, so the
-//                           flags sit at the same offset in every GPU's area)
-//   flags[16]               flags[g] = e: GPU g's rows of call e are here
+//                           (sized by rows_total, which every GPU shares, so
+//                           the copies sit at the same offset in every area)
 //   epoch                   the last call's epoch (this GPU's own counter)
-// row_gather_kernel, after the sampling kernels of call e: stores the staged
-// rows into copy e & 1 of every area over NVLink (one 8-byte store per row
-// and GPU), a CTA barrier, then one thread fences at system scope, releases
-// flags[me] = e on every GPU, waits (bounded, about 2 s) until its own
-// flags[] all reach e, and the CTA copies that copy to the caller's outputs.
-// A peer's copy e & 1 is free again when this GPU writes call e + 2: that
-// peer released flags = e + 1, which it does only after its own copy-out of
-// call e. A wait that gives up returns every row as -1 with
-// NCB_FLAG_PEER_TIMEOUT.
+// row_gather_kernel, after the sampling kernels of call e: stores each of its
+// rows as two 64-bit words tagged with e into copy e & 1 of every GPU's area
+// over NVLink, then polls its own copy until every word carries e (bounded,
+// about 2 s) and copies the rows out. A word is one single-copy-atomic 8-byte
+// access on both sides, so its tag proves its value is this call's: no fence,
+// no separate flag. A peer's copy e & 1 is free again when this GPU writes
+// call e + 2: this GPU finished call e + 1 only after every peer had stored
+// its e + 1 words, which each peer does after its own call e (copy-out
+// included) has completed. A word still stale after the wait makes its row
+// -1 with NCB_FLAG_PEER_TIMEOUT.
 #pragma once
 
 #include "peer_exchange.cuh"
@@ -31,17 +31,15 @@ constexpr int RG_THREADS = 256;
 
 struct RgLayout {
   size_t staging_off;  // bytes from the area base
-  size_t flags_off;
   size_t epoch_off;
   size_t bytes;
 };
 inline RgLayout rg_layout(int rows_total) {
   RgLayout l;
-  const size_t copies = (size_t)2 * rows_total * 8;
+  const size_t copies = (size_t)2 * rows_total * 16;
   l.staging_off = (copies + 255) / 256 * 256;
-  l.flags_off = l.staging_off + ((size_t)2 * rows_total * 4 + 255) / 256 * 256;
-  l.epoch_off = l.flags_off + 128;
-  l.bytes = l.flags_off + 256;
+  l.epoch_off = l.staging_off + ((size_t)2 * rows_total * 4 + 255) / 256 * 256;
+  l.bytes = l.epoch_off + 256;
   return l;
 }
 
@@ -53,9 +51,17 @@ struct RgArgs {
   uint32_t* out_flg;    // [rows_total], may be null
 };
 
+__device__ __forceinline__ void st_u64_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_u64_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __global__ void __launch_bounds__(RG_THREADS) row_gather_kernel(const __grid_constant__ RgArgs g) {
   __shared__ uint32_t s_epoch;
-  __shared__ int s_ok;
   // the sampling kernels (and their fix-up) come first on the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
@@ -64,35 +70,42 @@ __global__ void __launch_bounds__(RG_THREADS) row_gather_kernel(const __grid_con
   if (tid == 0) s_epoch = *epoch + 1u;
   __syncthreads();
   const uint32_t e = s_epoch;
-  const int c = (int)(e & 1u);
+  const size_t cbase = (size_t)(e & 1u) * g.rows_total * 2;  // in words
   const int32_t* st_tok = reinterpret_cast<const int32_t*>(own + g.l.staging_off);
   const uint32_t* st_flg = reinterpret_cast<const uint32_t*>(st_tok + g.rows_total);
+  const uint64_t tag = (uint64_t)e << 32;
   for (int i = tid; i < g.rows; i += RG_THREADS) {
-    const uint2 v = make_uint2((uint32_t)st_tok[i], st_flg[i]);
-    for (int p = 0; p < g.ranks; ++p)
-      reinterpret_cast<uint2*>(g.area[p])[(size_t)c * g.rows_total + g.row_begin + i] = v;
+    const uint64_t wt = tag | (uint32_t)st_tok[i];
+    const uint64_t wf = tag | st_flg[i];
+    const size_t w = cbase + (size_t)(g.row_begin + i) * 2;
+    for (int p = 0; p < g.ranks; ++p) {
+      uint64_t* c = reinterpret_cast<uint64_t*>(g.area[p]) + w;
+      st_u64_sys(c, wt);
+      st_u64_sys(c + 1, wf);
+    }
   }
-  // The barrier orders every thread's stores before thread 0's system fence
-  // and its releases (the barrier-then-one-fence pattern of a grid barrier).
-  __syncthreads();
-  if (tid == 0) {
-    // one fence, then relaxed flag stores: a release pattern for every flag
-    __threadfence_system();
-    for (int p = 0; p < g.ranks; ++p)
-      asm volatile("st.relaxed.sys.global.u32 [%0], %1;"
-                   ::"l"(reinterpret_cast<uint32_t*>(g.area[p] + g.l.flags_off) + g.me), "r"(e)
-                   : "memory");
-    s_ok = wait_words_bounded(reinterpret_cast<const uint32_t*>(own + g.l.flags_off), g.ranks, e)
-               ? 1 : 0;
-  }
-  __syncthreads();
-  const uint2* cp = reinterpret_cast<const uint2*>(own) + (size_t)c * g.rows_total;
+  // every row of the batch from the own copy, each word waited for (one
+  // deadline per thread, about 2 s)
+  const uint64_t* cp = reinterpret_cast<const uint64_t*>(own) + cbase;
+  uint64_t t0 = 0;
+  bool late = false;
   for (int i = tid; i < g.rows_total; i += RG_THREADS) {
-    uint2 v = make_uint2(0xffffffffu, FLAG_PEER_TIMEOUT);
-    if (s_ok) v = __ldcv(cp + i);
-    g.out_tok[i] = (int32_t)v.x;
-    if (g.out_flg) g.out_flg[i] = v.y;
+    uint64_t wt = ld_u64_sys(cp + 2 * i), wf = ld_u64_sys(cp + 2 * i + 1);
+    for (int it = 0; !late && ((uint32_t)(wt >> 32) != e || (uint32_t)(wf >> 32) != e); ++it) {
+      if ((it & 15) == 0) {
+        const uint64_t t = global_ns();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > 2000000000ull) late = true;
+      }
+      __nanosleep(100);
+      wt = ld_u64_sys(cp + 2 * i);
+      wf = ld_u64_sys(cp + 2 * i + 1);
+    }
+    const bool ok = (uint32_t)(wt >> 32) == e && (uint32_t)(wf >> 32) == e;
+    g.out_tok[i] = ok ? (int32_t)(uint32_t)wt : -1;
+    if (g.out_flg) g.out_flg[i] = ok ? (uint32_t)wf : FLAG_PEER_TIMEOUT;
   }
+  __syncthreads();
   if (tid == 0) *epoch = e;
 }
 
