@@ -254,14 +254,15 @@ NCB_API int ncb_logits_filter_top_p_device(NcbSampler* sampler, float* d_probs, 
  * caller gives every handle all handles in shard order
  * (ncb_vocab_shard_peer_connect; handles exported by the same process resolve
  * without IPC). Connect returns NCB_ERROR_INVALID_ARGUMENT unless every handle
- * was set up for the same shard count and the same max_rows. Per call, on every GPU in the same order:
- * ncb_vocab_shard_push_peer_device (shard kernel, then its records are stored
- * into every GPU's area over NVLink and an epoch flag is released there) and
- * ncb_vocab_shard_merge_peer_device (waits for every shard's flag, merges,
- * releases an ack that lets the peers overwrite its area on the next call).
- * Every wait is bounded (about 2 s); a merge that gives up returns token -1
- * with NCB_FLAG_PEER_TIMEOUT. rows <= the handle's max_rows; all GPUs pass the
- * same rows, vocab and params. */
+ * was set up for the same shard count and the same max_rows. Per call, on
+ * every GPU in the same order: ncb_vocab_shard_push_peer_device (the shard
+ * kernel; each finished record is stored, every word tagged with the call's
+ * epoch, into every GPU's area over NVLink) and
+ * ncb_vocab_shard_merge_peer_device (waits until every shard's words of the
+ * row carry the epoch, then merges). Every wait is bounded (about 2 s); a row
+ * whose words do not all arrive returns token -1 with NCB_FLAG_PEER_TIMEOUT.
+ * rows <= the handle's max_rows; all GPUs pass the same rows, vocab and
+ * params. */
 #define NCB_FLAG_PEER_TIMEOUT 0x80u
 NCB_API int ncb_peer_handle_bytes(void);
 NCB_API int ncb_vocab_shard_peer_setup(NcbSampler* sampler, int shards, int me, void* handle_out);

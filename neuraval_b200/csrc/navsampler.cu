@@ -989,14 +989,14 @@ static int launch_shard_candidates(NcbSampler* h, const float* d_logits, int row
   return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
 }
 
-// The merge kernel; with wait_flags it first waits for the peers' records of
-// `epoch` and finally releases acks[] (peer-memory exchange).
+// The merge kernel; with `tagged` (peer-memory exchange) it first waits for
+// this call's tagged record words and unpacks them into `unpack`.
 static int launch_merge(NcbSampler* h, const uint32_t* recs, int shards, int rows, int vocab,
                         const float* d_u, const NcbSamplerParams* prm, int32_t* d_tok,
-                        uint32_t* d_flags, const uint32_t* wait_flags,
-                        uint32_t* const* acks, cudaStream_t stream) {
+                        uint32_t* d_flags, const uint64_t* tagged, uint32_t* unpack,
+                        cudaStream_t stream) {
   nvs::MergeArgs m{};
-  m.recs = recs;
+  m.recs = tagged ? unpack : recs;
   m.shards = shards;
   m.rows = rows;
   m.a.V = vocab;
@@ -1005,10 +1005,11 @@ static int launch_merge(NcbSampler* h, const uint32_t* recs, int shards, int row
   m.a.tokens = d_tok;
   m.a.flags = d_flags;
   m.a.s = h->s;
-  m.wait_flags = wait_flags;
-  m.epoch = h->s.px_ticket + 3;
-  if (acks) {
-    for (int s = 0; s < shards; ++s) m.ack[s] = acks[s];
+  if (tagged) {
+    m.tagged = tagged;
+    m.unpack = unpack;
+    m.max_rows = h->max_rows;
+    m.epoch = h->s.px_ticket + 3;
     m.ticket = h->s.px_ticket + 2;
   }
   const size_t smem = nvs::vm_smem_bytes();
@@ -1200,18 +1201,13 @@ NCB_API int ncb_vocab_shard_push_peer_device(NcbSampler* h, const float* d_logit
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   h->px_pushed = true;
-  const size_t slot_bytes = (size_t)rows * nvs::VS_REC_WORDS * 4;
-  uint32_t* own = reinterpret_cast<uint32_t*>(h->px_area + (size_t)h->px_me * slot_bytes);
+  uint32_t* own = reinterpret_cast<uint32_t*>(h->px_area + h->px_layout.own_off);
   nvs::PxArgs px{};
-  for (int s = 0; s < h->px_shards; ++s) {
-    px.dst[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + (size_t)h->px_me * slot_bytes);
-    px.flag[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + h->px_layout.flags_off) + h->px_me;
-  }
-  px.acks = reinterpret_cast<const uint32_t*>(h->px_area + h->px_layout.acks_off);
-  px.ticket = h->s.px_ticket;
+  for (int s = 0; s < h->px_shards; ++s) px.tagged[s] = reinterpret_cast<uint64_t*>(h->px_base[s]);
   px.epoch = h->s.px_ticket + 3;
   px.shards = h->px_shards;
   px.me = h->px_me;
+  px.max_rows = h->max_rows;
   // the shard kernel stores each finished record into every peer's area itself
   st = launch_shard_candidates(h, d_logits, rows, vocab, col_begin, col_end, ld, d_hist,
                                d_hist_offsets, prm, own, stream, &px);
@@ -1233,14 +1229,11 @@ NCB_API int ncb_vocab_shard_merge_peer_device(NcbSampler* h, int rows, int vocab
   std::lock_guard<std::recursive_mutex> lk(h->mu);
   DeviceGuard g(h->device);
   if (!g.ok) return set_status(NCB_ERROR_INIT_FAILED);
-  uint32_t* acks[nvs::PX_MAX] = {};
-  for (int s = 0; s < h->px_shards; ++s)
-    if (s != h->px_me)
-      acks[s] = reinterpret_cast<uint32_t*>(h->px_base[s] + h->px_layout.acks_off) + h->px_me;
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(h->px_area + h->px_layout.flags_off);
-  return set_status(launch_merge(h, reinterpret_cast<const uint32_t*>(h->px_area), h->px_shards,
-                                 rows, vocab, d_uniforms, prm, d_tokens, d_flags, flags, acks,
-                                 static_cast<cudaStream_t>(stream_)));
+  return set_status(launch_merge(
+      h, nullptr, h->px_shards, rows, vocab, d_uniforms, prm, d_tokens, d_flags,
+      reinterpret_cast<const uint64_t*>(h->px_area),
+      reinterpret_cast<uint32_t*>(h->px_area + h->px_layout.plain_off),
+      static_cast<cudaStream_t>(stream_)));
 }
 
 }  // extern "C"

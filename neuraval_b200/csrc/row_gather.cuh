@@ -51,15 +51,6 @@ struct RgArgs {
   uint32_t* out_flg;    // [rows_total], may be null
 };
 
-__device__ __forceinline__ void st_u64_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_u64_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(RG_THREADS) row_gather_kernel(const __grid_constant__ RgArgs g) {
   __shared__ uint32_t s_epoch;
   // the sampling kernels (and their fix-up) come first on the stream

@@ -40,8 +40,8 @@ struct Scratch {
   int32_t* gi;          // [max_ctas]
   uint32_t* error_word; // [1] sticky error bits (timeouts)
   uint32_t* fixup;      // [max_rows]  1: row must be redone on the full-vocabulary path
-  uint32_t* px_ticket;  // [4] peer exchange: push CTAs, failed push waits, merge CTAs (zero
-                        // between launches), epoch of the last call
+  uint32_t* px_ticket;  // [4] peer exchange: [2] merge CTAs (zero between launches),
+                        // [3] epoch of the last merged call; [0], [1] unused
   uint32_t* stats;      // [1] rows redone by the full-sort kernel (null: not counted)
   uint2* ck_keys;       // chunked top-k: kept (raw value bits, column) per warp group,
                         // [rows][chunks][8 warps][16]

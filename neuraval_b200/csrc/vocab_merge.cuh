@@ -27,45 +27,60 @@ struct MergeArgs {
   int shards;
   int rows;
   SampleArgs a;          // V = full vocabulary, p, uniforms, tokens, flags (probs unused)
-  // peer-memory exchange only (null otherwise): wait until flags[0..shards)
-  // reach epoch, then release acks to every peer from the last CTA
-  const uint32_t* wait_flags;
-  const uint32_t* epoch;  // the push kernel's epoch word
-  uint32_t* ack[PX_MAX];
+  // peer-memory exchange only (null otherwise): this GPU's tagged words
+  // ([2][shards][max_rows][VS_REC_WORDS]), unpacked into recs (then writable)
+  // once every word of the row carries this call's epoch; the last CTA
+  // advances the epoch
+  const uint64_t* tagged;
+  uint32_t* unpack;      // = recs, writable
+  int max_rows;
+  uint32_t* epoch;       // local: the last merged call's epoch
   uint32_t* ticket;      // local, zero between launches
 };
 
 __device__ void merge_row(const MergeArgs& g);
 
 __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_constant__ MergeArgs g) {
-  __shared__ int s_ok, s_last;
-  __shared__ uint32_t s_epoch;
-  const int tid = threadIdx.x;
-  if (g.wait_flags) {
-    if (tid == 0) {
-      s_epoch = __ldcg(g.epoch);
-      s_ok = wait_words_bounded(g.wait_flags, g.shards, s_epoch) ? 1 : 0;
+  __shared__ int s_last;
+  const int tid = threadIdx.x, row = blockIdx.x;
+  if (g.tagged) {
+    const uint32_t e = __ldcg(g.epoch) + 1u;
+    // every word of this row's records, each waited for (one deadline per
+    // thread, about 2 s), unpacked into the plain layout merge_row reads
+    const uint64_t* src = g.tagged + (size_t)(e & 1u) * g.shards * g.max_rows * VS_REC_WORDS;
+    uint64_t t0 = 0;
+    bool ok = true;
+    for (int idx = tid; idx < g.shards * VS_REC_WORDS; idx += VM_THREADS) {
+      const int s = idx / VS_REC_WORDS, i = idx - s * VS_REC_WORDS;
+      const uint64_t* w = src + ((size_t)s * g.max_rows + row) * VS_REC_WORDS + i;
+      uint64_t v = ld_u64_sys(w);
+      for (int it = 0; ok && (uint32_t)(v >> 32) != e; ++it) {
+        if ((it & 15) == 0) {
+          const uint64_t t = global_ns();
+          if (t0 == 0) t0 = t;
+          else if (t - t0 > 2000000000ull) ok = false;
+        }
+        __nanosleep(100);
+        v = ld_u64_sys(w);
+      }
+      g.unpack[((size_t)s * g.rows + row) * VS_REC_WORDS + i] = (uint32_t)v;
     }
-    __syncthreads();
-    if (s_ok) {
+    if (__syncthreads_and(ok ? 1 : 0)) {
       merge_row(g);
     } else if (tid == 0) {
-      g.a.tokens[blockIdx.x] = -1;
-      if (g.a.flags) g.a.flags[blockIdx.x] = FLAG_PEER_TIMEOUT;
+      g.a.tokens[row] = -1;
+      if (g.a.flags) g.a.flags[row] = FLAG_PEER_TIMEOUT;
     }
-  } else {
-    merge_row(g);
-  }
-  if (g.ticket) {
+    // the last CTA advances the epoch (every CTA has read the words by then)
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(g.ticket, 1u) == gridDim.x - 1u;
     __syncthreads();
     if (s_last && tid == 0) {
-      __threadfence_system();
-      for (int s = 0; s < g.shards; ++s)
-        if (g.ack[s]) st_release_sys(g.ack[s], s_epoch);
+      *g.epoch = e;
       *g.ticket = 0u;
     }
+  } else {
+    merge_row(g);
   }
 }
 
