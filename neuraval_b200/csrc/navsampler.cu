@@ -208,6 +208,11 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::topk_chunk_finish_kernel<false, 4>);
   set((const void*)nvs::topk_chunk_finish_kernel<true, 8>);
   set((const void*)nvs::topk_chunk_finish_kernel<false, 8>);
+  set((const void*)nvs::topk_chunk_kernel<true>);
+  set((const void*)nvs::topk_chunk_finish_kernel<true, 4, true>);
+  set((const void*)nvs::topk_chunk_finish_kernel<false, 4, true>);
+  set((const void*)nvs::topk_chunk_finish_kernel<true, 8, true>);
+  set((const void*)nvs::topk_chunk_finish_kernel<false, 8, true>);
   set((const void*)nvs::fullvocab_fixup_kernel<true>);
   set((const void*)nvs::fullvocab_fixup_kernel<false>);
   set((const void*)nvs::filter_top_p_kernel);
@@ -968,6 +973,49 @@ static int launch_shard_candidates(NcbSampler* h, const float* d_logits, int row
   a.shard_out = records;
   const bool counts = (prm->frequency_penalty != 0.0f || prm->presence_penalty != 0.0f);
   a.h_cap = counts ? pow2_at_least(h->max_history > 0 ? h->max_history : 1) : 0;
+  // Wide shards with k <= 64 and lowering penalties: the chunked stream and
+  // finish kernels (the finish writes the records), then the shard kernel below
+  // in fix-up mode for the rows the finish could not prove.
+  const int K = prm->top_k < vocab ? prm->top_k : vocab;
+  const bool lowering = prm->repetition_penalty >= 1.0f && prm->frequency_penalty >= 0.0f &&
+                        prm->presence_penalty >= 0.0f;
+  const int J = nvs::ck_chunks(width);
+  const bool chunked = !prm->greedy && h->chunked && h->forced_splits == 0 && K < width &&
+                       K <= nvs::TL_KMAX && lowering && width >= 8192 && J <= h->ck_jmax &&
+                       683LL * K <= (long long)width;
+  if (chunked) {
+    a.bm_words = (width + 31) / 32 + 1;
+    const size_t fsmem = nvs::fk_smem_bytes(a.bm_words, a.h_cap);
+    const size_t ring = nvs::cr_smem_bytes();
+    if ((int)fsmem > h->max_dyn_smem || (int)ring > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const int nchunks = rows * J;
+    cudaLaunchConfig_t c1{};
+    c1.gridDim = dim3(nchunks < h->num_sms ? nchunks : h->num_sms);
+    c1.blockDim = dim3(nvs::CR_THREADS);
+    c1.dynamicSmemBytes = ring;
+    c1.stream = stream;
+    c1.attrs = attr;
+    c1.numAttrs = 1;
+    if (cudaLaunchKernelEx(&c1, nvs::topk_chunk_kernel<true>, a, J, nchunks) != cudaSuccess)
+      return NCB_ERROR_LAUNCH_FAILED;
+    cudaLaunchConfig_t c2 = c1;
+    c2.gridDim = dim3(rows);
+    c2.blockDim = dim3(nvs::FK_THREADS);
+    c2.dynamicSmemBytes = fsmem;
+    const bool wide = J * nvs::CK_WARPS * nvs::CK_KEYS > 4 * nvs::FK_THREADS;
+    cudaError_t e;
+    if (counts)
+      e = wide ? cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<true, 8, true>, a, J)
+               : cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<true, 4, true>, a, J);
+    else
+      e = wide ? cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<false, 8, true>, a, J)
+               : cudaLaunchKernelEx(&c2, nvs::topk_chunk_finish_kernel<false, 4, true>, a, J);
+    if (e != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
+    a.fixup_only = 1;
+  }
   int S = prm->greedy ? choose_splits(rows, width, h->num_sms, h->forced_splits)
                       : choose_splits_topk(rows, width, h->num_sms, h->forced_splits);
   a.seg_len = round_up((width + S - 1) / S, 4);
@@ -983,8 +1031,19 @@ static int launch_shard_candidates(NcbSampler* h, const float* d_logits, int row
   } else {
     const size_t smem = nvs::tl_smem_bytes(a.bm_words, a.h_cap);
     if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
-    if (counts) nvs::topk_ldg_kernel<true, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
-    else nvs::topk_ldg_kernel<false, true><<<grid, nvs::TL_THREADS, smem, stream>>>(a);
+    cudaLaunchConfig_t c{};
+    c.gridDim = grid;
+    c.blockDim = dim3(nvs::TL_THREADS);
+    c.dynamicSmemBytes = smem;
+    c.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = attr;
+    c.numAttrs = a.fixup_only ? 1 : 0;  // the fix-up follows the finish kernel closely
+    const cudaError_t e = counts ? cudaLaunchKernelEx(&c, nvs::topk_ldg_kernel<true, true>, a)
+                                 : cudaLaunchKernelEx(&c, nvs::topk_ldg_kernel<false, true>, a);
+    if (e != cudaSuccess) return NCB_ERROR_LAUNCH_FAILED;
   }
   return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
 }

@@ -375,7 +375,11 @@ inline size_t fk_smem_bytes(int bm_words, int h_cap) {
 // kept-value slots is thread tid's k-th: group s / CK_KEYS, place s % CK_KEYS,
 // so the 16 slots of a group are 16 consecutive lanes (loads coalesce, group
 // reductions are half-warp shuffles). FK_SLOTS * FK_THREADS >= G * CK_KEYS.
-template <bool kCounts, int FK_SLOTS>
+// kShard: the row is one GPU's columns [a.col_lo, a.col_hi) of a vocabulary
+// split; instead of sampling, the CTA writes the row's shard record (every
+// value >= the shard's K-th largest, ties included; shard_record.cuh) and
+// stores it into the peers' areas when a.px has peers.
+template <bool kCounts, int FK_SLOTS, bool kShard = false>
 __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const __grid_constant__ SampleArgs a, int J) {
   extern __shared__ __align__(128) unsigned char smem[];
   float* gtop = reinterpret_cast<float*>(smem);                        // [FK_THREADS]
@@ -400,6 +404,7 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   const int NT = G * M;
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
   const size_t gbase = (size_t)row * G;
+  const int lo = kShard ? a.col_lo : 0, hi = kShard ? a.col_hi : V;
 
   // Prologue on the call's inputs only (history, uniform): they were written
   // before the chunk kernel started, which itself waited for them, so this
@@ -413,11 +418,11 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
     s_vmax = 0u;
     s_slow[0] = 0u;
     s_slow[1] = 0u;
-    s_u = a.uniforms[row];
+    s_u = kShard ? 0.0f : a.uniforms[row];
   }
   Penalty P;
   const bool hist_ok =
-      setup_penalty_range<kCounts>(P, a, a.hoff[row], a.hoff[row + 1], 0, V, bitmap, hsorted, &s_hn);
+      setup_penalty_range<kCounts>(P, a, a.hoff[row], a.hoff[row + 1], lo, hi, bitmap, hsorted, &s_hn);
   const bool pen = P.rep || P.cnt;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -460,7 +465,8 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
       const float raw = __uint_as_float(kv[k].x);
       const int col = (int)kv[k].y;
       float av = raw;
-      if (pen && ((bitmap[col >> 5] >> (col & 31)) & 1u)) av = ck_adjust(P, raw, col);
+      const int rc = col - lo;  // the bitmap covers [lo, hi)
+      if (pen && ((bitmap[rc >> 5] >> (rc & 31)) & 1u)) av = ck_adjust(P, raw, col);
       ev = canon(__fmul_rn(av, scale));
       if (!(ev < INFINITY)) any |= 1u;  // scaled past the float range, as the reference's value
     }
@@ -513,7 +519,11 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   if (!hist_ok) state = FLAG_BAD_HISTORY;
   else if (anyall & 1u) state = FLAG_NONFINITE;
   if (state) {
-    if (tid == 0) {
+    if constexpr (kShard) {  // a record carrying the state: the merge returns -1
+      write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, gtop,
+                        reinterpret_cast<const int*>(cand), 0, state, -INFINITY);
+      if (a.px.shards > 0) shard_px_epilogue(a.px, a.shard_out + (size_t)row * VS_REC_WORDS, row, true);
+    } else if (tid == 0) {
       a.tokens[row] = -1;
       if (a.flags) a.flags[row] = state;
     }
@@ -579,13 +589,35 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
     }
     for (; h < nc; ++h) r += cand[h] > key;
     sorted[r] = key;
-    if (r < 64) {
+    if (!kShard && r < 64) {
       bool slow = false;
       w[r] = exp_cr(__fsub_rn(cand_val(key), vmax), slow);
       if (slow) atomicOr(&s_slow[r >> 5], 1u << (r & 31));
     }
   }
   __syncthreads();
+  if constexpr (kShard) {
+    // the K-th value T, proven as below; the record holds every candidate >= T
+    // (all of the shard's values >= T are candidates: they are above every
+    // dropped value, and L <= T)
+    const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);
+    if (s_bkey >= tk) {
+      if (tid == 0) a.s.fixup[row] = 1u;
+      return;
+    }
+    float* cv = gtop;                          // FK_THREADS >= FK_CAND floats
+    int* cid = reinterpret_cast<int*>(cand);   // FK_CAND ints (cand is free now)
+    int c = 0;
+    for (int i = tid; i < nc; i += FK_THREADS) {
+      cv[i] = cand_val(sorted[i]);
+      cid[i] = cand_id(sorted[i]);
+      if ((uint32_t)(sorted[i] >> 32) >= tk) ++c;
+    }
+    c = __syncthreads_count(c > 0 ? c : 0);  // nc <= FK_THREADS: one entry per thread
+    write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, cv, cid, c, 0u, kval(tk));
+    if (a.px.shards > 0) shard_px_epilogue(a.px, a.shard_out + (size_t)row * VS_REC_WORDS, row, true);
+    return;
+  }
   // warp 0: the K-th value, the proof, the candidates (ties included) and the finish
   if (warp == 0) {
     const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);

@@ -72,6 +72,7 @@ struct SampleArgs {
   int col_hi;
   uint32_t* shard_out;
   PxArgs px;            // peers of a shard kernel (px.shards == 0: none)
+  int fixup_only;       // topk_ldg_kernel: only rows with s.fixup[row] set, which it clears
 };
 
 constexpr int HIST_PRE = 4;  // history ids per thread loaded before any is used

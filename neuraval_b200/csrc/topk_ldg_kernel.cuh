@@ -222,6 +222,10 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
   // overlaps that kernel's end, and nothing is read before that kernel's
   // writes are visible (a no-op for an ordinary launch)
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // fix-up mode: rows the chunked finish kernel could not prove, nothing else
+  // (every segment of a row reads the same mark; the CTA that completes the
+  // row clears it, after every segment of the row has started)
+  if (a.fixup_only && __ldcg(a.s.fixup + blockIdx.y) == 0u) return;
   topk_ldg_body<kCounts, kShard>(a, &s_owner);
   if constexpr (kShard) {
     if (a.px.shards > 0) {
@@ -229,6 +233,10 @@ __global__ void __launch_bounds__(TL_THREADS, 2)
       shard_px_epilogue(a.px, a.shard_out + (size_t)blockIdx.y * VS_REC_WORDS, blockIdx.y,
                         s_owner != 0);
     }
+  }
+  if (a.fixup_only) {
+    __syncthreads();
+    if (s_owner != 0 && threadIdx.x == 0) a.s.fixup[blockIdx.y] = 0u;
   }
 }
 

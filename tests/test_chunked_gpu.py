@@ -146,3 +146,51 @@ def test_raising_penalty_and_probs_take_the_row_kernel(sampler, oracle):
     ot, of, op = run_oracle(oracle, wl, oracle.EXP_CR, want_probs=True)
     assert_exact(gt, gf, ot, of, "with probabilities")
     assert np.array_equal(gp, op)
+
+
+def test_vocab_shards_through_the_chunked_kernels(sampler, row_sampler, oracle):
+    """Shards of 40000 columns (two per 80000-column row) take the chunked
+    stream and finish kernels, the finish writing each row's shard record; rows
+    it cannot prove (top K in one warp's range, all values equal, fewer than K
+    finite values) are redone by the one-CTA-per-row shard kernel. The merged
+    tokens and flags equal those of the one-CTA-per-row shard kernel on every
+    row, and the oracle's on every row whose ties did not overflow a record."""
+    from tests.test_vocab_shard_gpu import run_sharded
+    rng = np.random.default_rng(29)
+    V = 80000
+    rows = []
+    base = rng.standard_normal(V).astype(np.float32) * 2
+    rows.append(base)
+    r = base.copy(); r[12345] = np.nan; rows.append(r)
+    r = base.copy(); r[V - 1] = np.inf; rows.append(r)
+    rows.append(np.zeros(V, np.float32))
+    r = np.full(V, -np.inf, np.float32); r[rng.choice(V, 20, replace=False)] = 1.0
+    rows.append(r)
+    r = np.where(rng.random(V) < 0.7, -np.inf, rng.standard_normal(V)).astype(np.float32)
+    rows.append(r)
+    for lo in (1000, 41000, 39990):  # top K inside one warp's range of either shard, or across
+        r = rng.standard_normal(V).astype(np.float32)
+        r[lo:lo + 64] += 20.0
+        rows.append(r)
+    r = rng.standard_normal(V).astype(np.float32)
+    r[0:3] = 9.0; r[-3:] = 9.5; r[39998:40002] = 9.2
+    rows.append(r)
+    logits = np.stack(rows)
+    B = logits.shape[0]
+    Hs = rng.integers(0, 60, B)
+    hist = np.concatenate([rng.integers(-5, V + 5, h) for h in Hs]).astype(np.int32)
+    hist[:3] = [777, 12345, V - 1]
+    offs = np.concatenate([[0], np.cumsum(Hs)]).astype(np.int32)
+    for params in (dict(temperature=0.7, top_p=0.8, top_k=50, repetition_penalty=1.3),
+                   dict(temperature=1.1, top_p=0.95, top_k=64, frequency_penalty=0.4,
+                        presence_penalty=0.2)):
+        wl = dict(name="shard edge", logits=logits, hist_ids=hist, hist_offsets=offs,
+                  uniforms=rng.random(B).astype(np.float32), params=params)
+        ct, cf = run_sharded(sampler, wl, 2)
+        rt, rf = run_sharded(row_sampler, wl, 2)
+        assert np.array_equal(ct, rt) and np.array_equal(cf, rf), (params, ct, rt, cf, rf)
+        ot, of, _ = run_oracle(oracle, wl, oracle.EXP_CR)
+        ok = (cf & native.FLAG_TIES_OVERFLOW) == 0
+        assert_exact(ct[ok], cf[ok], ot[ok], of[ok], "shard edge")
+        assert ok[[0, 1, 2, 5, 6, 7, 8, 9]].all()  # rows whose ties cannot overflow a record
+        assert ct[1] == -1 and ct[2] == -1  # NaN / +inf: -1 with NCB_FLAG_NONFINITE
