@@ -587,14 +587,19 @@ def e2e_rows(rs, args, world, dev):
     h_offs = torch.from_numpy((offs[lo: lo + rows + 1] - offs[lo]).astype(np.int32)).pin_memory()
     h_u = torch.from_numpy(np.ascontiguousarray(wl["uniforms"][lo: lo + rows])).pin_memory()
     hl, hh, ho, hu = (t.numpy() for t in (h_logits, h_hist, h_offs, h_u))
-    for _ in range(2):
-        rs.sampler.sample_rows(hl, hh, ho, hu, rs.params)
+    from neuraval_b200.sampler import CudaTokenSampler
+    # a handle of its own, as a caller of the host-array API would hold
+    sampler = CudaTokenSampler(device=dev.index, max_rows=max(1, rows), max_vocab=rs.V,
+                               max_history=max(1, rs.H))
+    for _ in range(3):
+        sampler.sample_rows(hl, hh, ho, hu, rs.params)
     if world > 1:
         torch.distributed.barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        rs.sampler.sample_rows(hl, hh, ho, hu, rs.params)
+        sampler.sample_rows(hl, hh, ho, hu, rs.params)
     e2e_s = time.perf_counter() - t0
+    sampler.close()
     # the host-to-device copy alone (pinned, one copy per step)
     d = torch.empty(h_logits.shape, dtype=torch.float32, device=dev)
     s = torch.cuda.Stream(dev)

@@ -89,6 +89,7 @@ struct NcbSampler {
   float* h_probs_dev = nullptr;
   size_t h_hist_cap = 0;
   cudaStream_t host_stream = nullptr;  // sampling and the copies out
+  int32_t* h_out_pinned = nullptr;     // [2][max_rows] tokens and flags on their way out
   cudaStream_t copy_stream = nullptr;  // the copies in, slice by slice
   cudaEvent_t slice_ev[8] = {};        // slice i of the logits is on the device
   // vocabulary shards exchanged through peer memory
@@ -402,6 +403,7 @@ NCB_API int ncb_sampler_destroy(NcbSampler* h) {
     cudaFree(h->h_probs_dev);
     if (h->host_stream) cudaStreamDestroy(h->host_stream);
     if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
+    if (h->h_out_pinned) cudaFreeHost(h->h_out_pinned);
     for (cudaEvent_t e : h->slice_ev)
       if (e) cudaEventDestroy(e);
   }
@@ -559,7 +561,8 @@ static bool ensure_staging(NcbSampler* h, size_t nh, bool probs) {
         cudaMalloc(&h->h_tok_dev, (size_t)h->max_rows * sizeof(int32_t)) != cudaSuccess ||
         cudaMalloc(&h->h_flags_dev, (size_t)h->max_rows * sizeof(uint32_t)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&h->host_stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMallocHost(&h->h_out_pinned, (size_t)h->max_rows * 2 * sizeof(int32_t)) != cudaSuccess)
       return false;
     for (cudaEvent_t& e : h->slice_ev)
       if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
@@ -674,16 +677,23 @@ NCB_API int ncb_sample_rows(NcbSampler* h, const float* h_logits, int rows, int 
       return set_status(st);
     }
   }
-  ok = cudaMemcpyAsync(h_tokens, h->h_tok_dev, (size_t)rows * sizeof(int32_t),
-                       cudaMemcpyDeviceToHost, s) == cudaSuccess;
+  // tokens and flags through the handle's pinned buffer (a copy into the
+  // caller's pageable memory would be staged by the driver), copied on the
+  // host after the synchronisation
+  int32_t* pt = h->h_out_pinned;
+  uint32_t* pf = reinterpret_cast<uint32_t*>(h->h_out_pinned + h->max_rows);
+  ok = cudaMemcpyAsync(pt, h->h_tok_dev, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                       s) == cudaSuccess;
   if (h_flags)
-    ok = ok && cudaMemcpyAsync(h_flags, h->h_flags_dev, (size_t)rows * sizeof(uint32_t),
+    ok = ok && cudaMemcpyAsync(pf, h->h_flags_dev, (size_t)rows * sizeof(uint32_t),
                                cudaMemcpyDeviceToHost, s) == cudaSuccess;
   if (h_probs)
     ok = ok && cudaMemcpyAsync(h_probs, h->h_probs_dev, (size_t)rows * vocab * sizeof(float),
                                cudaMemcpyDeviceToHost, s) == cudaSuccess;
   if (!ok) return set_status(NCB_ERROR_COPY_FAILED);
   if (cudaStreamSynchronize(s) != cudaSuccess) return set_status(NCB_ERROR_LAUNCH_FAILED);
+  std::memcpy(h_tokens, pt, (size_t)rows * sizeof(int32_t));
+  if (h_flags) std::memcpy(h_flags, pf, (size_t)rows * sizeof(uint32_t));
   return set_status(NCB_OK);
 }
 
