@@ -399,8 +399,10 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   const int K = min(a.p.top_k, V);
   const int G = J * CK_WARPS;
   // each group contributes its M largest exact values to the lower bound of
-  // the K-th value (G * M >= K distinct elements)
-  const int M = (K + G - 1) / G;
+  // the K-th value (G * M >= K distinct elements); with fewer than 2K groups,
+  // two per group keep the bound tight (one per group would make it the
+  // smallest group maximum, and let most kept values through as candidates)
+  const int M = max((K + G - 1) / G, 2 * K > G ? 2 : 1);
   const int NT = G * M;
   const float scale = __fdiv_rn(1.0f, a.p.temperature);  // TokenSampler.cs:68
   const size_t gbase = (size_t)row * G;
