@@ -93,7 +93,7 @@ struct NcbSampler {
   cudaStream_t copy_stream = nullptr;  // the copies in, slice by slice
   cudaEvent_t slice_ev[8] = {};        // slice i of the logits is on the device
   // vocabulary shards exchanged through peer memory
-  char* px_area = nullptr;  // this GPU's exchange area (records, flags, acks)
+  char* px_area = nullptr;  // this GPU's exchange area (tagged, unpacked and own records)
   int px_shards = 0, px_me = -1;
   bool px_connected = false;
   nvs::PeerLayout px_layout{};
@@ -1144,9 +1144,9 @@ NCB_API int ncb_vocab_shard_merge_device(NcbSampler* h, const void* d_records, i
 // ---- vocabulary shards through peer memory ------------------------------------
 //
 // The exchange of ncb_vocab_shard_* done by the library itself: the shard
-// kernel stores every finished record straight into the other GPUs' exchange
-// areas over NVLink (CUDA IPC mappings) and releases an epoch flag; the merge
-// waits for the flags and acks back. No collective, no extra kernel.
+// kernels store every finished record straight into every GPU's exchange area
+// over NVLink (CUDA IPC mappings), each word tagged with the call's epoch; the
+// merge waits for its row's words. No collective, no extra kernel.
 
 extern "C" {
 

@@ -133,9 +133,9 @@ class RowShardedSampler:
 
 class PeerRowShardedSampler(RowShardedSampler):
     """RowShardedSampler whose gather is done by the library through peer memory
-    (each GPU stores its rows' tokens and flags into every GPU's gather area
-    over NVLink and releases a per-call flag there) instead of an NCCL
-    all-gather. The process group is used once, to exchange the areas' IPC
+    (each GPU stores its rows' tokens and flags, tagged with the call's epoch,
+    into every GPU's gather area over NVLink and waits until its own area holds
+    every row of the call) instead of an NCCL all-gather. The process group is used once, to exchange the areas' IPC
     handles."""
 
     def __init__(self, sampler, rows: int, group=None):
@@ -223,8 +223,8 @@ class VocabShardedSampler:
 
 class PeerVocabShardedSampler(VocabShardedSampler):
     """VocabShardedSampler whose exchange is done by the library through peer
-    memory (records stored into every GPU's exchange area over NVLink, epoch
-    flags and acks) instead of an NCCL all-gather. The process group is used
+    memory (records stored into every GPU's exchange area over NVLink as
+    epoch-tagged words, waited for by the merge) instead of an NCCL all-gather. The process group is used
     once, to exchange the areas' IPC handles."""
 
     def __init__(self, sampler, vocab: int, group=None):
