@@ -1083,8 +1083,20 @@ static int launch_merge(NcbSampler* h, const uint32_t* recs, int shards, int row
   }
   const size_t smem = nvs::vm_smem_bytes();
   if ((int)smem > h->max_dyn_smem) return NCB_ERROR_CAPACITY;
-  nvs::vocab_merge_kernel<<<rows, nvs::VM_THREADS, smem, stream>>>(m);
-  return cudaGetLastError() == cudaSuccess ? NCB_OK : NCB_ERROR_LAUNCH_FAILED;
+  // with tagged words the merge may start polling while the shard kernels
+  // drain (a programmatic dependent launch); gathered records need stream order
+  cudaLaunchConfig_t c{};
+  c.gridDim = dim3(rows);
+  c.blockDim = dim3(nvs::VM_THREADS);
+  c.dynamicSmemBytes = smem;
+  c.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  c.attrs = attr;
+  c.numAttrs = tagged ? 1 : 0;
+  return cudaLaunchKernelEx(&c, nvs::vocab_merge_kernel, m) == cudaSuccess ? NCB_OK
+                                                                           : NCB_ERROR_LAUNCH_FAILED;
 }
 
 //

@@ -65,6 +65,10 @@ __global__ void __launch_bounds__(VM_THREADS) vocab_merge_kernel(const __grid_co
       }
       g.unpack[((size_t)s * g.rows + row) * VS_REC_WORDS + i] = (uint32_t)v;
     }
+    // launched as a programmatic dependent of the shard kernels (the words
+    // above need no ordering: their tags prove them); everything else this
+    // kernel reads was written before those kernels
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (__syncthreads_and(ok ? 1 : 0)) {
       merge_row(g);
     } else if (tid == 0) {
