@@ -375,6 +375,25 @@ inline size_t fk_smem_bytes(int bm_words, int h_cap) {
 // kept-value slots is thread tid's k-th: group s / CK_KEYS, place s % CK_KEYS,
 // so the 16 slots of a group are 16 consecutive lanes (loads coalesce, group
 // reductions are half-warp shuffles). FK_SLOTS * FK_THREADS >= G * CK_KEYS.
+// The shard record of a finished row: every candidate >= the K-th (sorted
+// holds the n candidates in descending order, all of the shard's values >= the
+// K-th among them), stored into the peers' areas when a.px has peers. Every
+// thread of the CTA calls; cv / cid are scratch for n entries.
+__device__ __forceinline__ void ck_shard_record(const SampleArgs& a, int row, int K, int n,
+                                                const uint64_t* sorted, float* cv, int* cid) {
+  const int tid = threadIdx.x;
+  const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);
+  int c = 0;
+  for (int i = tid; i < n; i += FK_THREADS) {
+    cv[i] = cand_val(sorted[i]);
+    cid[i] = cand_id(sorted[i]);
+    if ((uint32_t)(sorted[i] >> 32) >= tk) ++c;
+  }
+  c = __syncthreads_count(c > 0 ? c : 0);  // n <= FK_THREADS: one entry per thread
+  write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, cv, cid, c, 0u, kval(tk));
+  if (a.px.shards > 0) shard_px_epilogue(a.px, a.shard_out + (size_t)row * VS_REC_WORDS, row, true);
+}
+
 // kShard: the row is one GPU's columns [a.col_lo, a.col_hi) of a vocabulary
 // split; instead of sampling, the CTA writes the row's shard record (every
 // value >= the shard's K-th largest, ties included; shard_record.cuh) and
@@ -389,7 +408,7 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   float* wS = w + 64;                                                  // [64]
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(wS + 64);
   int32_t* hsorted = reinterpret_cast<int32_t*>(bitmap + a.bm_words);
-  __shared__ int s_hn, s_nc;
+  __shared__ int s_hn, s_nc, s_rescan;
   __shared__ uint32_t s_bkey, s_any, s_lkey, s_vmax, s_slow[2];
   __shared__ float s_u;
 
@@ -414,6 +433,7 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
   // are read after the wait below.
   if (tid == 0) {
     s_nc = 0;
+    s_rescan = 0;
     s_bkey = 0u;
     s_any = 0u;
     s_lkey = 0xFFFFFFFFu;
@@ -602,23 +622,11 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
     // the K-th value T, proven as below; the record holds every candidate >= T
     // (all of the shard's values >= T are candidates: they are above every
     // dropped value, and L <= T)
-    const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);
-    if (s_bkey >= tk) {
-      if (tid == 0) a.s.fixup[row] = 1u;
+    if (s_bkey < (uint32_t)(sorted[K - 1] >> 32)) {
+      ck_shard_record(a, row, K, nc, sorted, gtop, reinterpret_cast<int*>(cand));
       return;
     }
-    float* cv = gtop;                          // FK_THREADS >= FK_CAND floats
-    int* cid = reinterpret_cast<int*>(cand);   // FK_CAND ints (cand is free now)
-    int c = 0;
-    for (int i = tid; i < nc; i += FK_THREADS) {
-      cv[i] = cand_val(sorted[i]);
-      cid[i] = cand_id(sorted[i]);
-      if ((uint32_t)(sorted[i] >> 32) >= tk) ++c;
-    }
-    c = __syncthreads_count(c > 0 ? c : 0);  // nc <= FK_THREADS: one entry per thread
-    write_topk_record(a.shard_out + (size_t)row * VS_REC_WORDS, cv, cid, c, 0u, kval(tk));
-    if (a.px.shards > 0) shard_px_epilogue(a.px, a.shard_out + (size_t)row * VS_REC_WORDS, row, true);
-    return;
+    // unproven: the rescan below
   }
   // warp 0: the K-th value, the proof, the candidates (ties included) and the finish
   if (warp == 0) {
@@ -627,7 +635,92 @@ __global__ void __launch_bounds__(FK_THREADS, 2) topk_chunk_finish_kernel(const 
     const uint64_t k1 = lane + 32 < nc ? sorted[lane + 32] : 0ull;
     const bool over = nc > 64 && (uint32_t)(sorted[64] >> 32) == tk;  // > 64 candidates
     // every dropped value lies below the K-th value: it is the row's
-    if (s_bkey >= tk || over) {
+    if (over) {
+      if (lane == 0) a.s.fixup[row] = 1u;
+    } else if (s_bkey >= tk) {
+      if (lane == 0) s_rescan = 1;  // unproven: the rescan below
+    } else {
+      const unsigned b0 = __ballot_sync(0xffffffffu, k0 != 0ull && (uint32_t)(k0 >> 32) >= tk);
+      const unsigned b1 = __ballot_sync(0xffffffffu, k1 != 0ull && (uint32_t)(k1 >> 32) >= tk);
+      const int c = __popc(b0) + __popc(b1);
+      const bool any_slow = (s_slow[0] & b0) != 0u || (s_slow[1] & b1) != 0u;
+      finish_weights_warp(a, row, lane < c ? k0 : 0ull, lane + 32 < c ? k1 : 0ull, c, w, wS,
+                          any_slow, s_u);
+    }
+  }
+  if constexpr (!kShard) {
+    __syncthreads();
+    if (!s_rescan) return;
+  }
+  // A group held more of the row's top K than it kept, so a dropped value may
+  // lie above the K-th value. The CTA reads the whole row again (one column
+  // per lane and step: a rare path, placed after the common one) and takes
+  // every value >= L (at least K of them exist, whatever was dropped): the
+  // candidates are then complete without a proof; more than FK_CAND of them
+  // hand the row to the fix-up kernel.
+  __syncthreads();
+  if (tid == 0) {
+    s_nc = 0;
+    s_vmax = 0u;
+    s_slow[0] = 0u;
+    s_slow[1] = 0u;
+  }
+  __syncthreads();
+  {
+    const float* lrow = kShard ? a.logits + (size_t)row * a.ld - lo : a.logits + (size_t)row * V;
+    uint32_t vk2 = 0u;
+    for (int c0 = lo + warp * 32; c0 < hi; c0 += FK_THREADS) {
+      const int c = c0 + lane;
+      float ev = -INFINITY;
+      if (c < hi) {
+        const float raw = __ldcs(lrow + c);
+        const int rc = c - lo;
+        const float av = (pen && ((bitmap[rc >> 5] >> (rc & 31)) & 1u)) ? ck_adjust(P, raw, c) : raw;
+        ev = canon(__fmul_rn(av, scale));
+      }
+      const bool ok = ev >= L;
+      const unsigned b = __ballot_sync(0xffffffffu, ok);
+      if (b) {
+        const int leader = __ffs(b) - 1;
+        int base = 0;
+        if (lane == leader) base = atomicAdd(&s_nc, __popc(b));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        const int slot = base + __popc(b & ((1u << lane) - 1u));
+        if (ok && slot < FK_CAND) cand[slot] = cand_key(ev, c);
+        if (ok) vk2 = max(vk2, fkey(ev));
+      }
+    }
+    vk2 = __reduce_max_sync(0xffffffffu, vk2);
+    if (lane == 0 && vk2) atomicMax(&s_vmax, vk2);
+  }
+  __syncthreads();
+  const int n2 = s_nc;
+  if (n2 > FK_CAND || n2 < K) {
+    if (tid == 0) a.s.fixup[row] = 1u;
+    return;
+  }
+  {
+    const float vmax2 = kval(s_vmax);
+    if (tid < n2) {
+      const uint64_t key = cand[tid];
+      int r = 0;
+      for (int h = 0; h < n2; ++h) r += cand[h] > key;
+      sorted[r] = key;
+      if (!kShard && r < 64) {
+        bool slow = false;
+        w[r] = exp_cr(__fsub_rn(cand_val(key), vmax2), slow);
+        if (slow) atomicOr(&s_slow[r >> 5], 1u << (r & 31));
+      }
+    }
+  }
+  __syncthreads();
+  if constexpr (kShard) {
+    ck_shard_record(a, row, K, n2, sorted, gtop, reinterpret_cast<int*>(cand));
+  } else if (warp == 0) {
+    const uint32_t tk = (uint32_t)(sorted[K - 1] >> 32);
+    const uint64_t k0 = lane < n2 ? sorted[lane] : 0ull;
+    const uint64_t k1 = lane + 32 < n2 ? sorted[lane + 32] : 0ull;
+    if (n2 > 64 && (uint32_t)(sorted[64] >> 32) == tk) {  // > 64 candidates
       if (lane == 0) a.s.fixup[row] = 1u;
     } else {
       const unsigned b0 = __ballot_sync(0xffffffffu, k0 != 0ull && (uint32_t)(k0 >> 32) >= tk);

@@ -194,3 +194,23 @@ def test_vocab_shards_through_the_chunked_kernels(sampler, row_sampler, oracle):
         assert_exact(ct[ok], cf[ok], ot[ok], of[ok], "shard edge")
         assert ok[[0, 1, 2, 5, 6, 7, 8, 9]].all()  # rows whose ties cannot overflow a record
         assert ct[1] == -1 and ct[2] == -1  # NaN / +inf: -1 with NCB_FLAG_NONFINITE
+
+
+@pytest.mark.parametrize("at", [200, 70000, 127900])
+def test_clustered_top_k_rescans_instead_of_fix_up(sampler, oracle, at):
+    """Every row's 64 largest values inside one 1024-value group (as common
+    tokens with nearby ids can be): the finish cannot prove the K-th value from
+    the kept values, reads the row again, and still samples every row itself
+    (no row reaches the full-vocabulary fix-up); tokens equal the oracle's."""
+    rng = np.random.default_rng(31 + at)
+    B, V = 64, 128256
+    logits = rng.standard_normal((B, V), dtype=np.float32) * 2.0
+    logits[:, at:at + 64] += rng.uniform(6.0, 12.0, (B, 64)).astype(np.float32)
+    H = 128
+    hist = rng.integers(0, V, B * H).astype(np.int32)
+    hist[::7] = at + rng.integers(0, 64, hist[::7].size)  # penalised ids inside the cluster
+    wl = dict(name=f"clustered at {at}", logits=logits, hist_ids=hist,
+              hist_offsets=(np.arange(B + 1) * H).astype(np.int32),
+              uniforms=rng.random(B).astype(np.float32),
+              params=dict(temperature=0.9, top_p=0.9, top_k=50, repetition_penalty=1.2))
+    _check(sampler, oracle, wl, wl["name"], max_redone=0)
