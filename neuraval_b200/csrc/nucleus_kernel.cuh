@@ -81,8 +81,10 @@ struct NcSmem {
   uint32_t* qs;     // [NB] grid units of a normal bucket, then their exclusive prefix
   uint32_t* kq;     // [NB] straddling bucket: units of a weight below its half point;
                     // multi bucket: offset of its elements in the per-element pass
-  float* send;      // [NB] exact running sum after each bucket
-  float* regS;      // [NB+1] running sum at the start of each region
+  float* send;      // [NB+1] exact running sum after each bucket (before: pass 3's lower
+                    // threshold of each bucket)
+  float* regS;      // [NB+1] running sum at the start of each region (before: pass 3's
+                    // upper threshold of each bucket)
   uint16_t* splist; // [NB] special non-empty buckets, ascending
   uint16_t* soff;   // [NB] offset of each special bucket's elements in the walk's stage
   uint16_t* bk;     // [NB+1] binade of a normal bucket | NC_* flags (entry NB: 0)
@@ -93,8 +95,8 @@ struct NcSmem {
 };
 
 inline size_t nc_smem_bytes(int bm_words, int h_cap) {
-  return (size_t)(NC_NB + 1) * 4 + (size_t)(NC_NB + 4) * 4 + (size_t)NC_NB * 4 * 3 +
-         (size_t)(NC_NB + 1) * 4 + 8 +
+  return (size_t)(NC_NB + 1) * 4 + (size_t)(NC_NB + 4) * 4 + (size_t)NC_NB * 4 * 2 +
+         (size_t)(NC_NB + 1) * 4 * 2 + 8 +
          (size_t)NC_NB * 2 * 3 + (size_t)NC_NB / 32 * 4 * 2 + 64 +
          (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
@@ -106,7 +108,7 @@ __device__ __forceinline__ NcSmem nc_carve(unsigned char* smem, int bm_words) {
   s.cur = reinterpret_cast<uint32_t*>(p); p += (NC_NB + 4) * 4;
   s.qs = reinterpret_cast<uint32_t*>(p); p += NC_NB * 4;
   s.kq = reinterpret_cast<uint32_t*>(p); p += NC_NB * 4;
-  s.send = reinterpret_cast<float*>(p); p += NC_NB * 4;
+  s.send = reinterpret_cast<float*>(p); p += (NC_NB + 1) * 4;
   s.regS = reinterpret_cast<float*>(p); p += (NC_NB + 1) * 4;
   s.tie = reinterpret_cast<uint32_t*>(p); p += NC_NB / 32 * 4;
   s.gat = reinterpret_cast<uint32_t*>(p); p += NC_NB / 32 * 4;
@@ -719,6 +721,32 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
         if (cand[j] && !(s.bk[b] & (NC_SPECIAL | NC_EXCL))) s.bk[b] = (uint16_t)(s.bk[b] | NC_GATHER);
       }
     }
+    // pass 3's thresholds: a value x >= regS[b] adds one grid unit to the
+    // bucket, one in [send[b], regS[b]) goes the slow way (gathered, or a
+    // weight exactly at a straddling bucket's half point). A gathered bucket
+    // takes the slow way whole; a straddling one gathered too gets its units
+    // per element from its keys, like a multi bucket.
+#pragma unroll
+    for (int j = 0; j < NC_PER; ++j) {
+      const int b = tid * NC_PER + j;
+      uint32_t code = s.bk[b];
+      if (code & (NC_SPECIAL | NC_GATHER | NC_MULTI)) {
+        if (code & NC_STRADDLE) {
+          code = (code & ~NC_STRADDLE) | NC_MULTI;
+          s.bk[b] = (uint16_t)code;
+          s.qs[b] = 0u;
+        }
+        s.regS[b] = INFINITY;
+        s.send[b] = -INFINITY;
+      } else if (!(code & NC_STRADDLE)) {
+        s.regS[b] = INFINITY;
+        s.send[b] = INFINITY;
+      }
+    }
+    if (tid == 0) {  // values that never matter
+      s.regS[NC_NB] = INFINITY;
+      s.send[NC_NB] = INFINITY;
+    }
   }
   __syncthreads();
 
@@ -726,34 +754,40 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
   // the weights above their half point and note the ones exactly at it
   if (tid == 0) s_ntie = 0;
   __syncthreads();
-  // one value with its bucket and the bucket's code (NC_NB: code 0, nothing to do)
-  auto p3_one = [&](float v, int c, int b, uint32_t code) {
-    if (code & (NC_SPECIAL | NC_GATHER | NC_MULTI)) comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
-    if (code & NC_STRADDLE) {
-      const float x = __fsub_rn(v, vmax);
-      if (x >= s.regS[b]) {
-        atomicAdd(&s.qs[b], 1u);
-      } else if (x >= s.send[b]) {
-        const int i = atomicAdd(&s_ntie, 1);
-        if (i < NC_TIES) s_tlist[i] = (uint16_t)b;
-      }
+  // the slow way: a gathered bucket's key, or a weight at a half point
+  auto p3_slow = [&](float v, int c, int b) {
+    if (s.bk[b] & (NC_SPECIAL | NC_GATHER | NC_MULTI)) {
+      comp[atomicAdd(&s.cur[b], 1u)] = fv_comp(v, c);
+    } else {
+      const int i = atomicAdd(&s_ntie, 1);
+      if (i < NC_TIES) s_tlist[i] = (uint16_t)b;
     }
   };
   nc_stream4(
       lrow, V, P, scale,
       [&](float v, int c) {
         const int b = bin_rel(v);
-        p3_one(v, c, b, s.bk[b]);
+        const float x = __fsub_rn(v, vmax);
+        if (x >= s.regS[b]) atomicAdd(&s.qs[b], 1u);
+        else if (x >= s.send[b]) p3_slow(v, c, b);
       },
       [&](float v0, float v1, float v2, float v3, int c) {
         const int b0 = bin_rel(v0), b1 = bin_rel(v1), b2 = bin_rel(v2), b3 = bin_rel(v3);
-        const uint32_t k0 = s.bk[b0], k1 = s.bk[b1], k2 = s.bk[b2], k3 = s.bk[b3];
-        constexpr uint32_t kAny = NC_SPECIAL | NC_GATHER | NC_MULTI | NC_STRADDLE;
-        if ((k0 | k1 | k2 | k3) & kAny) {
-          p3_one(v0, c, b0, k0);
-          p3_one(v1, c + 1, b1, k1);
-          p3_one(v2, c + 2, b2, k2);
-          p3_one(v3, c + 3, b3, k3);
+        const float x0 = __fsub_rn(v0, vmax), x1 = __fsub_rn(v1, vmax);
+        const float x2 = __fsub_rn(v2, vmax), x3 = __fsub_rn(v3, vmax);
+        const float h0 = s.regS[b0], h1 = s.regS[b1], h2 = s.regS[b2], h3 = s.regS[b3];
+        const float l0 = s.send[b0], l1 = s.send[b1], l2 = s.send[b2], l3 = s.send[b3];
+        if (x0 >= h0) atomicAdd(&s.qs[b0], 1u);
+        if (x1 >= h1) atomicAdd(&s.qs[b1], 1u);
+        if (x2 >= h2) atomicAdd(&s.qs[b2], 1u);
+        if (x3 >= h3) atomicAdd(&s.qs[b3], 1u);
+        const bool w0 = x0 < h0 && x0 >= l0, w1 = x1 < h1 && x1 >= l1;
+        const bool w2 = x2 < h2 && x2 >= l2, w3 = x3 < h3 && x3 >= l3;
+        if (w0 | w1 | w2 | w3) {
+          if (w0) p3_slow(v0, c, b0);
+          if (w1) p3_slow(v1, c + 1, b1);
+          if (w2) p3_slow(v2, c + 2, b2);
+          if (w3) p3_slow(v3, c + 3, b3);
         }
       });
   __syncthreads();
