@@ -200,8 +200,10 @@ static bool raise_smem_limits(int limit) {
   set((const void*)nvs::greedy_kernel<true, true>);
   set((const void*)nvs::greedy_kernel<false, true>);
   set((const void*)nvs::vocab_merge_kernel);
-  set((const void*)nvs::nucleus_kernel<true>);
-  set((const void*)nvs::nucleus_kernel<false>);
+  set((const void*)nvs::nucleus_kernel<true, nvs::NcOne>);
+  set((const void*)nvs::nucleus_kernel<false, nvs::NcOne>);
+  set((const void*)nvs::nucleus_kernel<true, nvs::NcTwo>);
+  set((const void*)nvs::nucleus_kernel<false, nvs::NcTwo>);
   set((const void*)nvs::fullvocab_kernel<true>);
   set((const void*)nvs::fullvocab_kernel<false>);
   set((const void*)nvs::topk_chunk_kernel<false>);
@@ -546,7 +548,7 @@ static int launch_sample(NcbSampler* h, const float* d_logits, int rows, int V,
   // Full-vocabulary nucleus (no effective top-k) and very large top-k: the
   // bucketed kernel, with the full-sort kernel for the rows it hands over and
   // for calls that want the probabilities written.
-  if (!d_probs) return nvs::launch_nucleus(h->fv, a, rows, K, h->max_dyn_smem, stream);
+  if (!d_probs) return nvs::launch_nucleus(h->fv, a, rows, K, h->max_dyn_smem, h->num_sms, stream);
   return nvs::launch_fullvocab(h->fv, a, rows, K, h->max_dyn_smem, stream, false, 0);
 }
 

@@ -8,7 +8,7 @@
 // stays in one binade [2^e, 2^(e+1)), fl(S + w) = S + round(w / g) g with the
 // grid g = 2^(e-23): an integer addition whose order does not matter, except
 // for a weight exactly halfway between two grid points (its rounding follows
-// the parity of S). So one CTA per row:
+// the parity of S). So one CTA per row (its shape below):
 //   1. pass over the row: maximum and minimum of the penalised, scaled values;
 //   2. pass: histogram of x = v - max over NC_NB buckets spanning
 //      [max(min - max, -17), 0] (a weight below e^-17 < 2^-24 never changes a
@@ -39,19 +39,26 @@
 
 namespace nvs {
 
-#ifndef NC_THREADS_PER_CTA
-#define NC_THREADS_PER_CTA 1024
-#endif
-#ifndef NC_BUCKETS
-#define NC_BUCKETS 4096
-#endif
-#ifndef NC_CTAS_PER_SM
-#define NC_CTAS_PER_SM 1
-#endif
-constexpr int NC_THREADS = NC_THREADS_PER_CTA;
-constexpr int NC_NB = NC_BUCKETS;       // value buckets
-constexpr int NC_PER = NC_NB / NC_THREADS;
-constexpr int NC_WARPS = NC_THREADS / 32;
+// A CTA's shape: threads, value buckets, CTAs per SM. A batch that fits one
+// wave of SMs takes NcOne (1024 threads, 4096 buckets, one CTA per SM: the
+// row's latency decides); a larger one NcTwo (512 threads, 2560 buckets, two
+// CTAs per SM, so that one row's latency-bound phases - estimate, sorts, walk -
+// overlap the other's passes) when two of its CTAs fit an SM's shared memory.
+template <int kThreads, int kBuckets, int kCtasPerSm>
+struct NcShape {
+  static constexpr int T = kThreads, NB = kBuckets, PER = kBuckets / kThreads;
+  static constexpr int W = kThreads / 32, M = kCtasPerSm;
+  static_assert(kBuckets % kThreads == 0 && kBuckets % 32 == 0, "buckets: whole per thread");
+};
+using NcOne = NcShape<1024, 4096, 1>;
+using NcTwo = NcShape<512, 2560, 2>;
+// NcTwo's dynamic shared memory limit for two CTAs per SM (228 KB per SM, less
+// each CTA's static shared memory and reserve)
+constexpr size_t NC_TWO_SMEM_MAX = (size_t)110 << 10;
+// the shape's figures under the names the code below uses
+#define NC_SHAPE_NAMES                                                          \
+  constexpr int NC_THREADS = C::T, NC_NB = C::NB, NC_PER = C::PER, NC_WARPS = C::W; \
+  (void)NC_THREADS; (void)NC_NB; (void)NC_PER; (void)NC_WARPS
 constexpr int NC_SORT_WARP = 256;       // buckets up to this size are sorted by one warp
 constexpr int NC_SORT_BIG = 8192;       // a special bucket above this hands the row over
 // bk[]: the low byte holds a normal bucket's binade e (grid 2^(e-23)); flags:
@@ -65,7 +72,6 @@ constexpr uint32_t NC_MULTI = 0x0200u;    // several half points inside: gathere
 constexpr int NC_TIES = 64;               // such weights per row
 constexpr uint32_t NC_EMASK = 0x00FFu;
 constexpr uint32_t NC_QMAX = 1u << 23;  // a normal bucket's grid units stay below this
-constexpr int NC_QCAP = NC_NB;          // weights queued for the exact exp in one pass
 constexpr int NC_GATHER_CAP = 4096;     // elements of predicted cutoff / draw buckets
 
 // Bound on |__expf(x) - expf_correctly_rounded(x)| for x in [-17, 0], in ulps of
@@ -80,13 +86,13 @@ struct NcSmem {
                     // below e^-17 relative to the maximum, which never matter)
   uint32_t* qs;     // [NB] grid units of a normal bucket, then their exclusive prefix
   uint32_t* kq;     // [NB] straddling bucket: units of a weight below its half point;
-                    // multi bucket: offset of its elements in the per-element pass
+                    // multi bucket: offset of its elements in the per-element pass;
+                    // special bucket, after that: offset of its elements in the walk's stage
   float* send;      // [NB+1] exact running sum after each bucket (before: pass 3's lower
                     // threshold of each bucket)
   float* regS;      // [NB+1] running sum at the start of each region (before: pass 3's
                     // upper threshold of each bucket)
   uint16_t* splist; // [NB] special non-empty buckets, ascending
-  uint16_t* soff;   // [NB] offset of each special bucket's elements in the walk's stage
   uint16_t* bk;     // [NB+1] binade of a normal bucket | NC_* flags (entry NB: 0)
   uint32_t* tie;    // [NB/32] buckets holding an exact half (made special)
   uint32_t* gat;    // [NB/32] buckets to gather in the current pass
@@ -94,14 +100,18 @@ struct NcSmem {
   int32_t* hsorted;
 };
 
+template <class C>
 inline size_t nc_smem_bytes(int bm_words, int h_cap) {
+  NC_SHAPE_NAMES;
   return (size_t)(NC_NB + 1) * 4 + (size_t)(NC_NB + 4) * 4 + (size_t)NC_NB * 4 * 2 +
          (size_t)(NC_NB + 1) * 4 * 2 + 8 +
-         (size_t)NC_NB * 2 * 3 + (size_t)NC_NB / 32 * 4 * 2 + 64 +
+         (size_t)NC_NB * 2 * 2 + (size_t)NC_NB / 32 * 4 * 2 + 64 +
          (size_t)bm_words * 4 + (size_t)h_cap * 4;
 }
 
+template <class C>
 __device__ __forceinline__ NcSmem nc_carve(unsigned char* smem, int bm_words) {
+  NC_SHAPE_NAMES;
   NcSmem s;
   unsigned char* p = smem;
   s.pos = reinterpret_cast<uint32_t*>(p); p += (NC_NB + 1) * 4;
@@ -114,7 +124,6 @@ __device__ __forceinline__ NcSmem nc_carve(unsigned char* smem, int bm_words) {
   s.gat = reinterpret_cast<uint32_t*>(p); p += NC_NB / 32 * 4;
   s.bitmap = reinterpret_cast<uint32_t*>(p); p += (size_t)bm_words * 4;
   s.splist = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2;
-  s.soff = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2;
   s.bk = reinterpret_cast<uint16_t*>(p); p += NC_NB * 2 + 8;
   p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
   s.hsorted = reinterpret_cast<int32_t*>(p);
@@ -138,9 +147,10 @@ __device__ __forceinline__ float nc_adjust_member(const Penalty& P, float l, int
 // canonical value; 16-byte loads for the aligned body, NC_INFLIGHT of them
 // issued before any is used.
 constexpr int NC_INFLIGHT = 4;
-template <typename F>
+template <class C, typename F>
 __device__ __forceinline__ void nc_stream(const float* lrow, int V, const Penalty& P, float scale,
                                           F&& f) {
+  NC_SHAPE_NAMES;
   const bool pen = P.rep || P.cnt;
   auto val = [&](float l, bool member, int c) {
     return canon(__fmul_rn(member ? nc_adjust_member(P, l, c) : l, scale));
@@ -182,9 +192,10 @@ __device__ __forceinline__ void nc_stream(const float* lrow, int V, const Penalt
 
 // nc_stream with the aligned body handed over four values at a time:
 // f4(v0, v1, v2, v3, c) for columns c..c+3, f(v, c) for the unaligned ends.
-template <typename F, typename F4>
+template <class C, typename F, typename F4>
 __device__ __forceinline__ void nc_stream4(const float* lrow, int V, const Penalty& P, float scale,
                                            F&& f, F4&& f4) {
+  NC_SHAPE_NAMES;
   const bool pen = P.rep || P.cnt;
   auto val = [&](float l, bool member, int c) {
     return canon(__fmul_rn(member ? nc_adjust_member(P, l, c) : l, scale));
@@ -236,8 +247,9 @@ __device__ __noinline__ bool nc_units_exact(float x, float sc, uint32_t* q, int*
 
 // Exclusive block scan of one value per thread (NC_THREADS threads); returns
 // the thread's base and writes the total to *total. Ends synchronised.
-template <typename T>
+template <class C, typename T>
 __device__ __forceinline__ T nc_block_scan(T v, T* s_tmp, T* total) {
+  NC_SHAPE_NAMES;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   T inc = v;
 #pragma unroll
@@ -451,9 +463,10 @@ __device__ __forceinline__ int nc_first_ge(const float* a, int lo, int hi, float
   return lo;
 }
 
-template <bool kCounts>
-__global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
+template <bool kCounts, class C>
+__global__ void __launch_bounds__(C::T, C::M)
     nucleus_kernel(const __grid_constant__ SampleArgs a, FvScratch f, int K) {
+  NC_SHAPE_NAMES;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float s_fred[2][NC_WARPS];
   __shared__ uint32_t s_u32[33];
@@ -471,7 +484,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x;
   const int V = a.V;
-  NcSmem s = nc_carve(smem, a.bm_words);
+  NcSmem s = nc_carve<C>(smem, a.bm_words);
   const float* lrow = a.logits + (size_t)row * V;
   uint64_t* comp = f.comp + (size_t)row * f.max_vocab;
   float* ssum = f.ssum + (size_t)row * f.max_vocab;
@@ -502,7 +515,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
   {
     float mx = -INFINITY, mn = INFINITY;
     bool nf = false;
-    nc_stream(lrow, V, P, scale, [&](float v, int) {
+    nc_stream<C>(lrow, V, P, scale, [&](float v, int) {
       if (v != v || v == INFINITY) nf = true;
       mx = fmaxf(mx, v);
       mn = fminf(mn, v);
@@ -555,7 +568,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
     const float x = __fsub_rn(v, vmax);
     return x >= FV_XMIN ? bin(x) : NC_NB;
   };
-  nc_stream4(
+  nc_stream4<C>(
       lrow, V, P, scale, [&](float v, int) { atomicAdd(&s.cur[bin_rel(v)], 1u); },
       [&](float v0, float v1, float v2, float v3, int) {
         const int b0 = bin_rel(v0), b1 = bin_rel(v1), b2 = bin_rel(v2), b3 = bin_rel(v3);
@@ -576,7 +589,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       if (cnt[j]) atomicMax(&s_last, tid * NC_PER + j);
     }
     uint32_t total;
-    uint32_t run = nc_block_scan<uint32_t>(sum, s_u32, &total);
+    uint32_t run = nc_block_scan<C, uint32_t>(sum, s_u32, &total);
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       s.pos[tid * NC_PER + j] = run;
@@ -618,8 +631,8 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       }
     }
     double tl, th;
-    double lo = nc_block_scan<double>(clo, s_dbl, &tl);
-    double hi = nc_block_scan<double>(chi, s_dbl, &th);
+    double lo = nc_block_scan<C, double>(clo, s_dbl, &tl);
+    double hi = nc_block_scan<C, double>(chi, s_dbl, &th);
     double bl[NC_PER], bh[NC_PER];  // running sum bounds at each bucket's start / end
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
@@ -713,7 +726,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       if (cand[j]) ncand += cnt[j];
     }
     uint32_t ncand_tot;
-    (void)nc_block_scan<uint32_t>(ncand, s_u32, &ncand_tot);
+    (void)nc_block_scan<C, uint32_t>(ncand, s_u32, &ncand_tot);
     if (ncand_tot <= (uint32_t)NC_GATHER_CAP) {
 #pragma unroll
       for (int j = 0; j < NC_PER; ++j) {
@@ -763,7 +776,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       if (i < NC_TIES) s_tlist[i] = (uint16_t)b;
     }
   };
-  nc_stream4(
+  nc_stream4<C>(
       lrow, V, P, scale,
       [&](float v, int c) {
         const int b = bin_rel(v);
@@ -820,8 +833,8 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       sum += nm[j];
     }
     uint32_t tot, ntot;
-    uint32_t off = nc_block_scan<uint32_t>(sum, s_u32, &tot);
-    uint32_t li = nc_block_scan<uint32_t>(ism, s_u32, &ntot);
+    uint32_t off = nc_block_scan<C, uint32_t>(sum, s_u32, &tot);
+    uint32_t li = nc_block_scan<C, uint32_t>(ism, s_u32, &ntot);
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       const int b = tid * NC_PER + j;
@@ -880,8 +893,8 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       qsum += s.qs[b];
     }
     uint32_t nsp, qtot;
-    uint32_t o = nc_block_scan<uint32_t>(nsp_local, s_u32, &nsp);
-    uint32_t qrun = nc_block_scan<uint32_t>(qsum, s_u32, &qtot);
+    uint32_t o = nc_block_scan<C, uint32_t>(nsp_local, s_u32, &nsp);
+    uint32_t qrun = nc_block_scan<C, uint32_t>(qsum, s_u32, &qtot);
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       const int b = tid * NC_PER + j;
@@ -952,12 +965,12 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       sum += ne[j];
     }
     uint32_t total;
-    uint32_t run = nc_block_scan<uint32_t>(sum, s_u32, &total);
+    uint32_t run = nc_block_scan<C, uint32_t>(sum, s_u32, &total);
     staged = total <= (uint32_t)NC_NB;
 #pragma unroll
     for (int j = 0; j < NC_PER; ++j) {
       const int k = tid * NC_PER + j;
-      if (k < nsp && staged) s.soff[k] = (uint16_t)run;
+      if (k < nsp && staged && !(s.bk[s.splist[k]] & NC_TIEF)) s.kq[s.splist[k]] = run;
       run += ne[j];
     }
     __syncthreads();
@@ -968,7 +981,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
     for (int k = warp; k < nsp; k += NC_WARPS) {
       const int b = s.splist[k];
       const int p0 = (int)s.pos[b], n = n_walk(b);
-      float* w = staged ? stage + s.soff[k] : ssum + p0;
+      float* w = staged ? stage + (n ? s.kq[b] : 0u) : ssum + p0;
       for (int i = lane; i < n; i += 32) w[i] = exp_cr(__fsub_rn(fv_val(comp[p0 + i]), vmax), slow);
     }
     if (slow) s_slow = 1;
@@ -1035,7 +1048,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       const int bl = s.splist[k2];
       const int p0 = (int)s.pos[b0];
       const int len = (int)s.pos[bl] + n_eff(bl) - p0;
-      float* run = staged ? stage + s.soff[k] : ssum + p0;
+      float* run = staged ? stage + s.kq[b0] : ssum + p0;
       S = nc_warp_exact_run(run, len, S);
       for (int kk = k + lane; kk <= k2; kk += 32) {
         const int b = s.splist[kk];
@@ -1059,7 +1072,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
     for (int k = warp; k < nsp; k += NC_WARPS) {
       const int b = s.splist[k];
       const int p0 = (int)s.pos[b], n = n_walk(b);
-      for (int i = lane; i < n; i += 32) ssum[p0 + i] = stage[s.soff[k] + i];
+      for (int i = lane; i < n; i += 32) ssum[p0 + i] = stage[s.kq[b] + i];
     }
     __syncthreads();
   }
@@ -1218,7 +1231,7 @@ __global__ void __launch_bounds__(NC_THREADS, NC_CTAS_PER_SM)
       for (int b = tid; b <= last; b += NC_THREADS)
         if (marked(b) && !(s.bk[b] & (NC_GATHER | NC_MULTI))) s.cur[b] = s.pos[b];
       __syncthreads();
-      nc_stream(lrow, V, P, scale, [&](float v, int c) {
+      nc_stream<C>(lrow, V, P, scale, [&](float v, int c) {
         const float x = __fsub_rn(v, vmax);
         if (!(x >= FV_XMIN)) return;
         const int b = bin(x);
@@ -1334,17 +1347,34 @@ __global__ void fast_exp_steps_kernel(uint32_t k0, uint32_t k1, uint32_t* out) {
   if ((threadIdx.x & 31) == 0) atomicMax(out, worst);
 }
 
+template <class C>
+inline int launch_nucleus_shape(const FvScratch& f, const SampleArgs& a, int rows, int K,
+                                size_t smem, cudaStream_t stream) {
+  const bool counts = (a.p.frequency_penalty != 0.0f || a.p.presence_penalty != 0.0f);
+  if (counts) nucleus_kernel<true, C><<<rows, C::T, smem, stream>>>(a, f, K);
+  else nucleus_kernel<false, C><<<rows, C::T, smem, stream>>>(a, f, K);
+  return cudaGetLastError() == cudaSuccess ? 0 : 5;
+}
+
+// Rows that fit one wave of SMs run one 1024-thread CTA per SM; more rows run
+// two 512-thread CTAs per SM where two fit (else the one-CTA shape again).
 inline int launch_nucleus(const FvScratch& f, SampleArgs a, int rows, int K, int max_smem,
-                          cudaStream_t stream) {
+                          int num_sms, cudaStream_t stream) {
   if (a.V > f.max_vocab) return 8;  // NCB_ERROR_CAPACITY
   a.seg_len = a.V;
   a.bm_words = (a.V + 31) / 32 + 1;
   const bool counts = (a.p.frequency_penalty != 0.0f || a.p.presence_penalty != 0.0f);
-  const size_t smem = nc_smem_bytes(a.bm_words, counts ? a.h_cap : 0);
-  if ((int)smem > max_smem) return 8;
-  if (counts) nucleus_kernel<true><<<rows, NC_THREADS, smem, stream>>>(a, f, K);
-  else nucleus_kernel<false><<<rows, NC_THREADS, smem, stream>>>(a, f, K);
-  if (cudaGetLastError() != cudaSuccess) return 5;
+  const int h_cap = counts ? a.h_cap : 0;
+  const size_t smem_two = nc_smem_bytes<NcTwo>(a.bm_words, h_cap);
+  int st;
+  if (rows > num_sms && smem_two <= NC_TWO_SMEM_MAX) {
+    st = launch_nucleus_shape<NcTwo>(f, a, rows, K, smem_two, stream);
+  } else {
+    const size_t smem = nc_smem_bytes<NcOne>(a.bm_words, h_cap);
+    if ((int)smem > max_smem) return 8;  // NCB_ERROR_CAPACITY
+    st = launch_nucleus_shape<NcOne>(f, a, rows, K, smem, stream);
+  }
+  if (st != 0) return st;
   // rows a check handed over
   return launch_fullvocab(f, a, rows, K, max_smem, stream, true, 8);
 }

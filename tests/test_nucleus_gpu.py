@@ -47,7 +47,7 @@ def test_high_entropy_nucleus_rows(gpu_sampler, oracle):
           "high_entropy_nucleus 64x151936")
 
 
-@pytest.mark.parametrize("V,sigma,temperature,top_p", [
+DISTRIBUTIONS = [
     (32000, 0.05, 1.0, 0.9),     # nearly flat: every value relevant, dense buckets
     (32000, 6.0, 0.6, 0.95),     # very peaked: few relevant values
     (50257, 2.0, 1.3, 0.8),
@@ -55,15 +55,67 @@ def test_high_entropy_nucleus_rows(gpu_sampler, oracle):
     (151936, 0.3, 1.0, 0.99),
     (151936, 3.0, 0.8, 0.5),
     (262144, 1.5, 1.1, 0.97),
-])
-def test_distributions(gpu_sampler, oracle, V, sigma, temperature, top_p):
+]
+
+
+def _distribution(V, sigma, temperature, top_p):
     rng = np.random.default_rng(V + int(sigma * 100))
     logits, hist, offs = _rows(24, V, rng, sigma, 128)
     params = dict(temperature=temperature, top_p=top_p, top_k=native.INT_MAX,
                   repetition_penalty=1.2, presence_penalty=0.1)
-    wl = dict(logits=logits, hist_ids=hist, hist_offsets=offs,
-              uniforms=rng.random(24).astype(np.float32), params=params)
-    check(gpu_sampler, oracle, wl, f"V={V} sigma={sigma} T={temperature} p={top_p}")
+    return dict(logits=logits, hist_ids=hist, hist_offsets=offs,
+                uniforms=rng.random(24).astype(np.float32), params=params)
+
+
+@pytest.mark.parametrize("V,sigma,temperature,top_p", DISTRIBUTIONS)
+def test_distributions(gpu_sampler, oracle, V, sigma, temperature, top_p):
+    check(gpu_sampler, oracle, _distribution(V, sigma, temperature, top_p),
+          f"V={V} sigma={sigma} T={temperature} p={top_p}")
+
+
+def _tiled(wl, copies):
+    """The batch repeated `copies` times (rows, histories and uniforms)."""
+    B = wl["logits"].shape[0]
+    offs = np.asarray(wl["hist_offsets"])
+    lens = np.tile(np.diff(offs), copies)
+    return dict(logits=np.tile(wl["logits"], (copies, 1)),
+                hist_ids=np.tile(np.asarray(wl["hist_ids"])[:offs[B]], copies),
+                hist_offsets=np.concatenate([[0], np.cumsum(lens)]).astype(np.int32),
+                uniforms=np.tile(wl["uniforms"], copies), params=wl["params"])
+
+
+@pytest.mark.parametrize("case", [f"dist{i}" for i in range(len(DISTRIBUTIONS))] +
+                         ["high_entropy", "zipf_history", "top_k_1500"])
+def test_batch_shapes_agree(gpu_sampler, case):
+    """A batch of at most one row per SM runs one 1024-thread CTA per SM, a
+    larger one two 512-thread CTAs per SM with fewer, wider buckets (where two
+    fit an SM's shared memory): the same rows give the same tokens and flags
+    either way (the small batch is checked against the oracle by the tests
+    above)."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if case.startswith("dist"):
+        wl = _distribution(*DISTRIBUTIONS[int(case[4:])])
+    elif case == "high_entropy":
+        wl = workloads.high_entropy_nucleus(B=64, seed=11)
+    elif case == "zipf_history":
+        wl = workloads.zipf_history_nucleus()
+    else:
+        rng = np.random.default_rng(1500)
+        logits, hist, offs = _rows(24, 128256, rng, 1.0, 256)
+        wl = dict(logits=logits, hist_ids=hist, hist_offsets=offs,
+                  uniforms=rng.random(24).astype(np.float32),
+                  params=dict(temperature=0.8, top_p=0.9, top_k=1500, repetition_penalty=1.1))
+    B = wl["logits"].shape[0]
+    assert B <= sms
+    copies = sms // B + 1
+    before = gpu_sampler.full_sort_rows()
+    st, sf, _ = run_gpu(gpu_sampler, wl)
+    bt, bf, _ = run_gpu(gpu_sampler, _tiled(wl, copies))
+    assert gpu_sampler.full_sort_rows() == before, case
+    assert len(bt) == B * copies > sms
+    np.testing.assert_array_equal(bt, np.tile(st, copies), err_msg=case)
+    np.testing.assert_array_equal(bf, np.tile(sf, copies), err_msg=case)
 
 
 @pytest.mark.parametrize("top_k,top_p", [(1500, 0.9), (2000, 1.0), (40000, 0.95)])
