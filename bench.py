@@ -591,28 +591,32 @@ def e2e_rows(rs, args, world, dev):
     # a handle of its own, as a caller of the host-array API would hold
     sampler = CudaTokenSampler(device=dev.index, max_rows=max(1, rows), max_vocab=rs.V,
                                max_history=max(1, rs.H))
-    for _ in range(3):
-        sampler.sample_rows(hl, hh, ho, hu, rs.params)
-    if world > 1:
-        torch.distributed.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        sampler.sample_rows(hl, hh, ho, hu, rs.params)
-    e2e_s = time.perf_counter() - t0
-    sampler.close()
-    # the host-to-device copy alone (pinned, one copy per step)
+    # the host-to-device copy alone (pinned, one copy per step), timed step by
+    # step alternately with the call so that both see the same link (the PCIe
+    # bandwidth of a shared host drifts between runs)
     d = torch.empty(h_logits.shape, dtype=torch.float32, device=dev)
     s = torch.cuda.Stream(dev)
-    with torch.cuda.stream(s):
-        d.copy_(h_logits, non_blocking=True)
-        s.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
+
+    def h2d():
+        with torch.cuda.stream(s):
             d.copy_(h_logits, non_blocking=True)
             s.synchronize()
-        h2d_s = time.perf_counter() - t0
+
+    for _ in range(3):
+        sampler.sample_rows(hl, hh, ho, hu, rs.params)
+        h2d()
+    if world > 1:
+        torch.distributed.barrier()
+    e2e_s = h2d_s = 0.0
+    for _ in range(args.e2e_steps):
+        t0 = time.perf_counter()
+        sampler.sample_rows(hl, hh, ho, hu, rs.params)
+        t1 = time.perf_counter()
+        h2d()
+        t2 = time.perf_counter()
+        e2e_s += t1 - t0
+        h2d_s += t2 - t1
+    sampler.close()
     e2e_s, h2d_s = sharding.max_over_ranks([e2e_s, h2d_s], dev)
     B = rs.B
     return {"value": B * args.e2e_steps / e2e_s, "unit": UNIT,
